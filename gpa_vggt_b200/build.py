@@ -1,0 +1,75 @@
+"""Build the sm_100a shared library ``libgpa_b200.so`` in-tree with nvcc.
+
+The library exposes the C ABI declared in ``include/gpa_b200.h``.  It is built
+for ``sm_100a`` only (B200); nvcc cross-compiles it without a GPU present.
+
+    python -m gpa_vggt_b200.build          # build if sources changed
+    python -m gpa_vggt_b200.build --force  # rebuild
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = PKG / "csrc"
+LIB = PKG / "libgpa_b200.so"
+HEADER = ROOT / "include" / "gpa_b200.h"
+
+SOURCES = ["merge.cu", "sim_argmax.cu", "attention.cu", "frame.cu"]
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+    "--expt-relaxed-constexpr",
+]
+
+
+def _nvcc() -> str:
+    cand = [os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"]
+    for c in cand:
+        if c and Path(c).exists():
+            return c
+    raise RuntimeError("nvcc not found: set NVCC or put the CUDA toolkit on PATH")
+
+
+def _stale() -> bool:
+    if not LIB.exists():
+        return True
+    t = LIB.stat().st_mtime
+    deps = [CSRC / s for s in SOURCES] + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + [HEADER]
+    return any(d.stat().st_mtime > t for d in deps)
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    """Compile every CUDA source into one shared library (in-tree)."""
+    if not force and not _stale():
+        return LIB
+    nvcc = _nvcc()
+    tmp = LIB.with_suffix(".so.tmp")
+    cmd = [nvcc, *NVCC_FLAGS, "-shared", "-o", str(tmp), *[str(CSRC / s) for s in SOURCES]]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
+    os.replace(tmp, LIB)
+    return LIB
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("-v", "--verbose", action="store_true")
+    a = ap.parse_args(argv)
+    print(build(force=a.force, verbose=a.verbose))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

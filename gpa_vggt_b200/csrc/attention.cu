@@ -1,0 +1,384 @@
+// Flash attention with a per-key additive bias on the 5th-generation tensor
+// cores (head_dim 64, bf16 in, fp32 accumulate).
+//
+// Reference: merging/fused_attention.py:70-180 (_attn_keybias_kernel and
+// attention_keybias): o = softmax(q k^T * scale + bias) v with an online
+// softmax in the exp2 domain; optional log2 row sums lse = m + log2(l).
+//
+// B200 design (one CTA = two 128-query tiles of one (batch, head)):
+//   warp 0      TMA producer: Q tiles once, then K/V tiles through a 3-stage
+//               ring; also stages the tile's bias row (x log2 e, -inf past n).
+//   warp 1      one thread issues tcgen05.mma: S_t = Q_t K^T into TMEM and
+//               O_t += P_t V into TMEM, ping-ponging the two query tiles so the
+//               tensor core works on one tile while the other is in softmax.
+//   warps 2-9   two softmax warpgroups (one per query tile; thread == row):
+//               read S from TMEM, online softmax with lazy rescaling (the
+//               running max is only moved when it grows by more than 2^8),
+//               write P as bf16 into 128B-swizzled shared memory (the layout
+//               the MMA reads), rescale O in TMEM when the max moved, and
+//               finally normalise O and store it.
+#include "common.cuh"
+#include "capi_util.h"
+
+namespace gpa {
+namespace attn {
+
+constexpr int BM = 128;   // queries per tile
+constexpr int BN = 128;   // keys per tile
+constexpr int HD = 64;    // head dim
+constexpr int STAGES = 3;
+constexpr int TILE_BYTES = BM * HD * 2;  // 16 KB
+constexpr int P_BYTES = BM * BN * 2;     // 32 KB (two 16 KB swizzled chunks)
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+struct Smem {
+  static constexpr int Q = 0;                               // 2 x 16 KB
+  static constexpr int K = Q + 2 * TILE_BYTES;              // STAGES x 16 KB
+  static constexpr int V = K + STAGES * TILE_BYTES;         // STAGES x 16 KB
+  static constexpr int P = V + STAGES * TILE_BYTES;         // 2 x 32 KB
+  static constexpr int BIAS = P + 2 * P_BYTES;              // STAGES x 512 B
+  static constexpr int BARS = BIAS + STAGES * BN * 4;
+  static constexpr int TOTAL = BARS + 256;
+  static constexpr int ALLOC = TOTAL + 1024;
+};
+
+constexpr int THREADS = 320;
+constexpr int TMEM_COLS = 512;  // S0 0..127, S1 128..255, O0 256..319, O1 320..383
+
+struct Params {
+  int m, n, heads;
+  float scale_log2;
+  const float* bias;
+  int64_t bias_sb, bias_sh;
+  __nv_bfloat16* o;
+  int64_t o_sb, o_sh, o_sm;
+  float* lse;
+  int64_t lse_sb, lse_sh;
+  int* status;
+};
+
+__global__ void __launch_bounds__(THREADS)
+    attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                const __grid_constant__ CUtensorMap map_v, const Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Smem::BARS);
+  uint64_t* q_full = bars;                 // 1
+  uint64_t* kv_full = bars + 1;            // STAGES
+  uint64_t* kv_empty = kv_full + STAGES;   // STAGES
+  uint64_t* s_full = kv_empty + STAGES;    // 2
+  uint64_t* s_empty = s_full + 2;          // 2
+  uint64_t* p_full = s_empty + 2;          // 2
+  uint64_t* o_done = p_full + 2;           // 2
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* sbias = reinterpret_cast<float*>(smem + Smem::BIAS);
+
+  const int warp = warp_id(), lane = lane_id();
+  const int bh = blockIdx.y;
+  const int b = bh / p.heads, h = bh - b * p.heads;
+  const int q0 = blockIdx.x * (2 * BM);
+  const int nk = (p.n + BN - 1) / BN;
+
+  if (threadIdx.x == 0) {
+    bar_init(q_full, 1);
+    for (int s = 0; s < STAGES; ++s) {
+      bar_init(&kv_full[s], 1);
+      bar_init(&kv_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      bar_init(&s_full[t], 1);
+      bar_init(&s_empty[t], 4);
+      bar_init(&p_full[t], 4);
+      bar_init(&o_done[t], 1);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------ producer ------------------------------
+    const float* brow = p.bias ? p.bias + (int64_t)b * p.bias_sb + (int64_t)h * p.bias_sh : nullptr;
+    int issued = 0;
+    if (lane == 0) {
+      tma_prefetch_desc(&map_q);
+      tma_prefetch_desc(&map_k);
+      tma_prefetch_desc(&map_v);
+      bar_expect_tx(q_full, 2 * TILE_BYTES);
+      tma_load_4d(&map_q, q_full, smem + Smem::Q, 0, q0, h, b);
+      tma_load_4d(&map_q, q_full, smem + Smem::Q + TILE_BYTES, 0, q0 + BM, h, b);
+    }
+    for (int j = 0; j < nk; ++j) {
+      const int s = j % STAGES;
+      const uint32_t ph = (j / STAGES) & 1;
+      bool okw = wait_bar(&kv_empty[s], ph ^ 1, abort_flag, p.status, kDevTimeout);
+      if (!__all_sync(0xffffffffu, okw)) break;
+      float* bt = sbias + s * BN;
+#pragma unroll
+      for (int i = 0; i < BN / 32; ++i) {
+        const int c = i * 32 + lane;
+        const int col = j * BN + c;
+        float v = -INFINITY;
+        if (col < p.n) v = brow ? brow[col] * 1.4426950408889634f : 0.0f;
+        bt[c] = v;
+      }
+      __syncwarp();
+      if (lane == 0) {
+        bar_expect_tx(&kv_full[s], 2 * TILE_BYTES);
+        tma_load_4d(&map_k, &kv_full[s], smem + Smem::K + s * TILE_BYTES, 0, j * BN, h, b);
+        tma_load_4d(&map_v, &kv_full[s], smem + Smem::V + s * TILE_BYTES, 0, j * BN, h, b);
+      }
+      issued = j + 1;
+    }
+    if (lane == 0) {  // drain copies in flight before the CTA can exit
+      const unsigned long long t0 = global_ns();
+      drain_bar(q_full, 0, t0);
+      for (int j = max(0, issued - STAGES); j < issued; ++j)
+        drain_bar(&kv_full[j % STAGES], (j / STAGES) & 1, t0);
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer ------------------------------
+    if (elect_one()) {
+      constexpr uint32_t idesc_s = idesc_bf16(BM, BN, false, false);
+      constexpr uint32_t idesc_o = idesc_bf16(BM, HD, false, true);
+      const uint32_t sQ = smem_u32(smem + Smem::Q);
+      const uint32_t sK = smem_u32(smem + Smem::K);
+      const uint32_t sV = smem_u32(smem + Smem::V);
+      const uint32_t sP = smem_u32(smem + Smem::P);
+      auto issue_s = [&](int t, int j) {
+        const uint32_t kaddr = sK + (j % STAGES) * TILE_BYTES;
+        const uint32_t qaddr = sQ + t * TILE_BYTES;
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k)
+          umma_bf16(tbase + t * BN, sdesc_sw128(qaddr + k * 32, 16, 1024),
+                    sdesc_sw128(kaddr + k * 32, 16, 1024), idesc_s, k != 0);
+        umma_commit(&s_full[t]);
+      };
+      auto issue_o = [&](int t, int j) {
+        const uint32_t vaddr = sV + (j % STAGES) * TILE_BYTES;
+        const uint32_t paddr = sP + t * P_BYTES;
+#pragma unroll
+        for (int ks = 0; ks < BN / 16; ++ks)
+          umma_bf16(tbase + 256 + t * HD,
+                    sdesc_sw128(paddr + (ks >> 2) * TILE_BYTES + (ks & 3) * 32, 16, 1024),
+                    sdesc_sw128(vaddr + ks * 2048, 16384, 1024), idesc_o, (j > 0 || ks > 0));
+        umma_commit(&o_done[t]);
+      };
+      bool okw = wait_bar(q_full, 0, abort_flag, p.status, kDevTimeout) &&
+                 wait_bar(&kv_full[0], 0, abort_flag, p.status, kDevTimeout);
+      if (okw) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+      }
+      for (int j = 0; okw && j < nk; ++j) {
+        const bool more = j + 1 < nk;
+        // O0 += P0 V_j ; then S0 for the next tile
+        if (!(okw = wait_bar(&p_full[0], j & 1, abort_flag, p.status, kDevTimeout))) break;
+        tc_fence_after();
+        issue_o(0, j);
+        if (more) {
+          if (!(okw = wait_bar(&kv_full[(j + 1) % STAGES], ((j + 1) / STAGES) & 1, abort_flag,
+                               p.status, kDevTimeout)))
+            break;
+          if (!(okw = wait_bar(&s_empty[0], j & 1, abort_flag, p.status, kDevTimeout))) break;
+          tc_fence_after();
+          issue_s(0, j + 1);
+        }
+        // O1 += P1 V_j ; release the K/V stage ; then S1 for the next tile
+        if (!(okw = wait_bar(&p_full[1], j & 1, abort_flag, p.status, kDevTimeout))) break;
+        tc_fence_after();
+        issue_o(1, j);
+        umma_commit(&kv_empty[j % STAGES]);
+        if (more) {
+          if (!(okw = wait_bar(&s_empty[1], j & 1, abort_flag, p.status, kDevTimeout))) break;
+          tc_fence_after();
+          issue_s(1, j + 1);
+        }
+      }
+    }
+  } else {
+    // ------------------------------ softmax ------------------------------
+    const int t = (warp - 2) >> 2;       // query tile of this warpgroup
+    const int quad = warp & 3;           // TMEM lane quadrant
+    const int r = quad * 32 + lane;      // row within the tile
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t tS = tbase + lane_off + t * BN;
+    const uint32_t tO = tbase + lane_off + 256 + t * HD;
+    uint8_t* sP = smem + Smem::P + t * P_BYTES;
+    float m_ref = -INFINITY, l = 0.f;
+    bool okw = true;
+    for (int j = 0; j < nk; ++j) {
+      const int s = j % STAGES;
+      okw = wait_bar(&s_full[t], j & 1, abort_flag, p.status, kDevTimeout) &&
+            wait_bar(&kv_full[s], (j / STAGES) & 1, abort_flag, p.status, kDevTimeout);
+      if (!__all_sync(0xffffffffu, okw)) { okw = false; break; }
+      tc_fence_after();
+      float x[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) tmem_ld32f(tS + c * 32, x + c * 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) bar_arrive(&s_empty[t]);
+
+      const float4* bt = reinterpret_cast<const float4*>(sbias + s * BN);
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN / 4; ++c) {
+        float4 bb = bt[c];
+        x[4 * c + 0] = fmaf(x[4 * c + 0], p.scale_log2, bb.x);
+        x[4 * c + 1] = fmaf(x[4 * c + 1], p.scale_log2, bb.y);
+        x[4 * c + 2] = fmaf(x[4 * c + 2], p.scale_log2, bb.z);
+        x[4 * c + 3] = fmaf(x[4 * c + 3], p.scale_log2, bb.w);
+        mt = fmaxf(mt, fmaxf(fmaxf(x[4 * c], x[4 * c + 1]), fmaxf(x[4 * c + 2], x[4 * c + 3])));
+      }
+      float alpha = 1.f;
+      const bool moved = mt > m_ref + kRescaleThreshold;
+      if (moved) {
+        alpha = fast_exp2(m_ref - mt);  // 0 on the first tile (m_ref = -inf)
+        l *= alpha;
+        m_ref = mt;
+      }
+      // P_t and O_t are free once the previous O_t += P_t V finished
+      if (j > 0) {
+        okw = wait_bar(&o_done[t], (j - 1) & 1, abort_flag, p.status, kDevTimeout);
+        if (!__all_sync(0xffffffffu, okw)) { okw = false; break; }
+        tc_fence_after();
+      }
+      // P row -> shared memory, 128B swizzle, K-major (chunk = 64 keys)
+      float rs = 0.f;
+#pragma unroll
+      for (int u = 0; u < BN / 8; ++u) {
+        const int chunk = u >> 3, uu = u & 7;
+        float e[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          e[i] = fast_exp2(x[8 * u + i] - m_ref);
+          rs += e[i];
+        }
+        uint4 pk;
+        pk.x = pack_bf16x2(e[0], e[1]);
+        pk.y = pack_bf16x2(e[2], e[3]);
+        pk.z = pack_bf16x2(e[4], e[5]);
+        pk.w = pack_bf16x2(e[6], e[7]);
+        *reinterpret_cast<uint4*>(sP + chunk * TILE_BYTES + r * 128 + ((uu ^ (r & 7)) << 4)) = pk;
+      }
+      l += rs;
+      // rescale O_t in TMEM where the running max moved
+      if (j > 0 && __any_sync(0xffffffffu, moved)) {
+        uint32_t ov[32];
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          tmem_ld32(tO + hf * 32, ov);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+          tmem_st16(tO + hf * 32, ov);
+          tmem_st16(tO + hf * 32 + 16, ov + 16);
+        }
+        tmem_wait_st();
+      }
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) bar_arrive(&p_full[t]);
+    }
+    // epilogue
+    if (okw) {
+      okw = wait_bar(&o_done[t], (nk - 1) & 1, abort_flag, p.status, kDevTimeout);
+      okw = __all_sync(0xffffffffu, okw);
+    }
+    if (okw) {
+      tc_fence_after();
+      uint32_t ov[HD];
+      tmem_ld32(tO, ov);
+      tmem_ld32(tO + 32, ov + 32);
+      tmem_wait_ld();
+      const int row = q0 + t * BM + r;
+      if (row < p.m && !*abort_flag) {
+        const float inv = 1.0f / l;
+        __nv_bfloat16* orow = p.o + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)row * p.o_sm;
+#pragma unroll
+        for (int u = 0; u < HD / 8; ++u) {
+          uint4 pk;
+          pk.x = pack_bf16x2(__uint_as_float(ov[8 * u + 0]) * inv, __uint_as_float(ov[8 * u + 1]) * inv);
+          pk.y = pack_bf16x2(__uint_as_float(ov[8 * u + 2]) * inv, __uint_as_float(ov[8 * u + 3]) * inv);
+          pk.z = pack_bf16x2(__uint_as_float(ov[8 * u + 4]) * inv, __uint_as_float(ov[8 * u + 5]) * inv);
+          pk.w = pack_bf16x2(__uint_as_float(ov[8 * u + 6]) * inv, __uint_as_float(ov[8 * u + 7]) * inv);
+          reinterpret_cast<uint4*>(orow)[u] = pk;
+        }
+        if (p.lse) p.lse[(int64_t)b * p.lse_sb + (int64_t)h * p.lse_sh + row] = m_ref + __log2f(l);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, TMEM_COLS);
+  }
+}
+
+static int make_map4(CUtensorMap* map, const void* base, int n_rows, int heads, int batch,
+                     int64_t s_row, int64_t s_h, int64_t s_b, const char* what) {
+  // dims: (head_dim, rows, heads, batch); unused dims get a harmless stride
+  uint64_t dims[4] = {(uint64_t)HD, (uint64_t)n_rows, (uint64_t)heads, (uint64_t)batch};
+  uint64_t st[4] = {2, (uint64_t)s_row * 2, (uint64_t)s_h * 2, (uint64_t)s_b * 2};
+  if (heads == 1) st[2] = (uint64_t)n_rows * s_row * 2;
+  if (batch == 1) st[3] = st[2] * (uint64_t)heads;
+  if (st[1] == 0 || st[2] == 0 || st[3] == 0)
+    return fail(GPA_ERR_UNSUPPORTED, "%s: zero (broadcast) strides are not supported", what);
+  uint32_t box[4] = {HD, BM, 1, 1};
+  return make_map_bf16(map, base, 4, dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B, what);
+}
+
+}  // namespace attn
+}  // namespace gpa
+
+extern "C" int gpa_attention_keybias(const void* q, const void* k, const void* v, const float* bias,
+                                     int batch, int heads, int m, int n, int head_dim, int64_t q_sb,
+                                     int64_t q_sh, int64_t q_sm, int64_t k_sb, int64_t k_sh,
+                                     int64_t k_sn, int64_t v_sb, int64_t v_sh, int64_t v_sn,
+                                     int64_t bias_sb, int64_t bias_sh, float sm_scale, void* o,
+                                     int64_t o_sb, int64_t o_sh, int64_t o_sm, float* lse,
+                                     int64_t lse_sb, int64_t lse_sh, int* status, void* stream) {
+  using namespace gpa;
+  using namespace gpa::attn;
+  if (head_dim != HD) return fail(GPA_ERR_UNSUPPORTED, "gpa_attention_keybias: head_dim must be 64");
+  if (batch <= 0 || heads <= 0 || m < 0 || n <= 0)
+    return fail(GPA_ERR_INVALID, "gpa_attention_keybias: bad sizes");
+  if (!q || !k || !v || !o) return fail(GPA_ERR_INVALID, "gpa_attention_keybias: null pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+    return fail(GPA_ERR_INVALID, "gpa_attention_keybias: q/k/v/o must be 16-byte aligned");
+  if (o_sm % 8 || o_sh % 8 || o_sb % 8)
+    return fail(GPA_ERR_INVALID, "gpa_attention_keybias: o strides must be multiples of 8");
+  if (m == 0) return ok();
+  if ((int64_t)batch * heads > 65535)
+    return fail(GPA_ERR_UNSUPPORTED, "gpa_attention_keybias: batch*heads > 65535");
+  CUtensorMap mq, mk, mv;
+  int rc = make_map4(&mq, q, m, heads, batch, q_sm, q_sh, q_sb, "gpa_attention_keybias(q)");
+  if (!rc) rc = make_map4(&mk, k, n, heads, batch, k_sn, k_sh, k_sb, "gpa_attention_keybias(k)");
+  if (!rc) rc = make_map4(&mv, v, n, heads, batch, v_sn, v_sh, v_sb, "gpa_attention_keybias(v)");
+  if (rc) return rc;
+  Params p;
+  p.m = m; p.n = n; p.heads = heads;
+  p.scale_log2 = sm_scale * 1.4426950408889634f;
+  p.bias = bias; p.bias_sb = bias_sb; p.bias_sh = bias_sh;
+  p.o = (__nv_bfloat16*)o; p.o_sb = o_sb; p.o_sh = o_sh; p.o_sm = o_sm;
+  p.lse = lse; p.lse_sb = lse_sb; p.lse_sh = lse_sh;
+  p.status = status;
+  cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::ALLOC);
+  dim3 grid((m + 2 * BM - 1) / (2 * BM), batch * heads);
+  attn_kernel<<<grid, THREADS, Smem::ALLOC, (cudaStream_t)stream>>>(mq, mk, mv, p);
+  return check_launch("gpa_attention_keybias");
+}

@@ -1,0 +1,219 @@
+"""Torch-facing wrappers of the C ABI: validate tensors, allocate outputs,
+launch on the current stream.  One function per entry point of
+``include/gpa_b200.h``; the reference-shaped API lives in ``merging/`` and
+``layers/`` on top of these.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import call, ptr, stream_of, require_cuda, aligned
+
+BF16 = torch.bfloat16
+F32 = torch.float32
+
+
+def _dt(t: torch.Tensor) -> int:
+    if t.dtype == F32:
+        return _lib.GPA_DTYPE_F32
+    if t.dtype == BF16:
+        return _lib.GPA_DTYPE_BF16
+    raise TypeError(f"unsupported dtype {t.dtype} (bf16 or fp32)")
+
+
+def _tma_ok(t: torch.Tensor) -> bool:
+    """Innermost dim contiguous, other strides multiples of 8 elements, 16B base."""
+    if t.stride(-1) != 1 or not aligned(t):
+        return False
+    return all(s % 8 == 0 for s, n in zip(t.stride()[:-1], t.shape[:-1]) if n > 1)
+
+
+def sim_argmax(a: torch.Tensor, b: torch.Tensor, status: Optional[torch.Tensor] = None):
+    """node_max [B,M] fp32, node_idx [B,M] int32 of a [B,M,D] vs b [B,N,D] (bf16)."""
+    require_cuda(a, b, what="sim_argmax")
+    if a.dtype != BF16 or b.dtype != BF16:
+        raise TypeError("sim_argmax: a and b must be bf16")
+    if not _tma_ok(a):
+        a = a.contiguous()
+    if not _tma_ok(b):
+        b = b.contiguous()
+    B, M, D = a.shape
+    N = b.shape[1]
+    node_max = torch.empty(B, M, device=a.device, dtype=F32)
+    node_idx = torch.empty(B, M, device=a.device, dtype=torch.int32)
+    call("gpa_sim_argmax", ptr(a), ptr(b), B, M, N, D, a.stride(0), a.stride(1), b.stride(0),
+         b.stride(1), ptr(node_max), ptr(node_idx), ptr(status), stream_of(a))
+    return node_max, node_idx
+
+
+def merge_counts(num_imgs, w, h, sx, sy, num_special, no_rand):
+    nd, ns = ctypes.c_int(), ctypes.c_int()
+    call("gpa_merge_counts", num_imgs, w, h, sx, sy, num_special, int(bool(no_rand)),
+         ctypes.byref(nd), ctypes.byref(ns))
+    return nd.value, ns.value
+
+
+def merge_roles(rand_idx: Optional[torch.Tensor], num_imgs, w, h, sx, sy, num_special, no_rand,
+                device):
+    """dst_pos [num_dst], src_pos [num_src], slot [N] (int32, device)."""
+    nd, ns = merge_counts(num_imgs, w, h, sx, sy, num_special, no_rand)
+    N = nd + ns
+    dst_pos = torch.empty(nd, device=device, dtype=torch.int32)
+    src_pos = torch.empty(max(ns, 1), device=device, dtype=torch.int32)
+    slot = torch.empty(N, device=device, dtype=torch.int32)
+    if rand_idx is not None:
+        require_cuda(rand_idx, what="merge_roles")
+        rand_idx = rand_idx.to(torch.int64).contiguous()
+    call("gpa_merge_roles", ptr(rand_idx), num_imgs, w, h, sx, sy, num_special,
+         int(bool(no_rand)), ptr(dst_pos), ptr(src_pos), ptr(slot),
+         _lib._vp(torch.cuda.current_stream(device).cuda_stream))
+    return dst_pos, src_pos[:ns], slot
+
+
+def metric_split(metric: torch.Tensor, src_pos, dst_pos):
+    """Row-normalised bf16 a (src rows) and b (dst rows) of metric [N, d]."""
+    require_cuda(metric, what="metric_split")
+    if metric.stride(-1) != 1 or metric.stride(0) % 8 or not aligned(metric):
+        metric = metric.contiguous()
+    N, d = metric.shape
+    ns, nd = src_pos.numel(), dst_pos.numel()
+    a = torch.empty(ns, d, device=metric.device, dtype=BF16)
+    b = torch.empty(nd, d, device=metric.device, dtype=BF16)
+    call("gpa_metric_split", ptr(metric), _dt(metric), metric.stride(0), d, ptr(src_pos), ns,
+         ptr(dst_pos), nd, ptr(a), ptr(b), stream_of(metric))
+    return a, b
+
+
+@dataclass
+class MergePlan:
+    """Device arrays describing one bipartite merge (B == 1)."""
+    num_src: int
+    num_dst: int
+    r: int
+    dst_pos: torch.Tensor     # [num_dst] int32, absolute positions of dst tokens
+    src_pos: torch.Tensor     # [num_src] int32, absolute positions of src tokens
+    unm_src: torch.Tensor     # [num_src - r] int32, unmerged src ordinals
+    seg_start: torch.Tensor   # [num_dst + 1] int32
+    seg_src: torch.Tensor     # [r] int32
+    counts: torch.Tensor      # [N_m] fp32
+    node_max: Optional[torch.Tensor] = None
+    node_idx: Optional[torch.Tensor] = None
+
+    @property
+    def unm_len(self) -> int:
+        return self.num_src - self.r
+
+    @property
+    def n_out(self) -> int:
+        return self.unm_len + self.num_dst
+
+
+def merge_plan(node_max, node_idx, r: int, dst_pos, src_pos) -> MergePlan:
+    require_cuda(node_max, node_idx, what="merge_plan")
+    dev = node_max.device
+    ns, nd = src_pos.numel(), dst_pos.numel()
+    r = max(0, min(int(r), ns))
+    unm = torch.empty(max(ns - r, 1), device=dev, dtype=torch.int32)
+    seg_start = torch.empty(nd + 1, device=dev, dtype=torch.int32)
+    seg_src = torch.empty(max(r, 1), device=dev, dtype=torch.int32)
+    counts = torch.empty(ns - r + nd, device=dev, dtype=F32)
+    wsb = _lib.load().gpa_merge_plan_workspace_bytes(ns, nd)
+    ws = torch.empty(wsb, device=dev, dtype=torch.uint8)
+    nmx = node_max.reshape(-1).contiguous() if ns else node_max
+    nix = node_idx.reshape(-1).to(torch.int32).contiguous() if ns else node_idx
+    call("gpa_merge_plan", ptr(nmx), ptr(nix), ns, nd, r, ptr(unm), ptr(seg_start), ptr(seg_src),
+         ptr(counts), ptr(ws), wsb, stream_of(counts))
+    return MergePlan(ns, nd, r, dst_pos, src_pos, unm[: ns - r], seg_start, seg_src[:r], counts,
+                     node_max, node_idx)
+
+
+def merge_kv(t: torch.Tensor, plan: MergePlan, mean: bool = True, out: Optional[torch.Tensor] = None,
+             log_counts: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Merge t [H, N, D] (any strides, innermost contiguous) -> [H, N_m, D]."""
+    require_cuda(t, what="merge_kv")
+    H, N, D = t.shape
+    if t.stride(-1) != 1 or t.stride(0) % 8 or t.stride(1) % 8 or not aligned(t):
+        t = t.contiguous()
+    if out is None:
+        out = torch.empty(H, plan.n_out, D, device=t.device, dtype=t.dtype)
+    call("gpa_merge_kv_mean", ptr(t), _dt(t), H, N, D, t.stride(0), t.stride(1), ptr(plan.src_pos),
+         ptr(plan.dst_pos), ptr(plan.unm_src), plan.unm_len, ptr(plan.seg_start), ptr(plan.seg_src),
+         plan.num_dst, int(mean), ptr(log_counts), ptr(out), out.stride(0), out.stride(1),
+         stream_of(t))
+    return out
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bias: Optional[torch.Tensor],
+              sm_scale: float, return_lse: bool = False, out: Optional[torch.Tensor] = None,
+              status: Optional[torch.Tensor] = None):
+    """softmax(q k^T * scale + bias) v for q [B,H,M,64], k/v [B,H,N,64] bf16;
+    bias fp32 broadcastable to [B,H,N] (natural-log domain) or None."""
+    require_cuda(q, k, v, bias, what="attention")
+    for t in (q, k, v):
+        if t.dtype != BF16:
+            raise TypeError("attention: q, k, v must be bf16")
+    if not _tma_ok(q):
+        q = q.contiguous()
+    if not _tma_ok(k):
+        k = k.contiguous()
+    if not _tma_ok(v):
+        v = v.contiguous()
+    B, H, M, D = q.shape
+    N = k.shape[2]
+    bsb = bsh = 0
+    if bias is not None:
+        if bias.dtype != F32:
+            bias = bias.float()
+        bias = bias.reshape(bias.shape[0], bias.shape[1], N) if bias.dim() == 4 else bias
+        if bias.stride(-1) != 1:
+            bias = bias.contiguous()
+        bias = bias.expand(B, H, N)
+        bsb, bsh = bias.stride(0), bias.stride(1)
+    if out is None:
+        out = torch.empty(B, H, M, D, device=q.device, dtype=BF16)
+    lse = torch.empty(B, H, M, device=q.device, dtype=F32) if return_lse else None
+    call("gpa_attention_keybias", ptr(q), ptr(k), ptr(v), ptr(bias), B, H, M, N, D,
+         q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
+         v.stride(0), v.stride(1), v.stride(2), bsb, bsh, float(sm_scale), ptr(out),
+         out.stride(0), out.stride(1), out.stride(2), ptr(lse),
+         lse.stride(0) if lse is not None else 0, lse.stride(1) if lse is not None else 0,
+         ptr(status), stream_of(q))
+    return (out, lse) if return_lse else out
+
+
+def frame_pool(k: torch.Tensor, v: torch.Tensor, num_frames: int, ph: int, pw: int,
+               num_special: int, kp: int):
+    """Pooled k, v [H, S*npool, 64] bf16 and pool_size [H, S*npool] fp32 from
+    k, v [H, S*P, 64] bf16."""
+    require_cuda(k, v, what="frame_pool")
+    H, N, D = k.shape
+    if k.stride(-1) != 1 or k.stride(1) % 8 or k.stride(0) % 8 or not aligned(k):
+        k = k.contiguous()
+    if v.stride() != k.stride() or not aligned(v):
+        v = v.contiguous()
+        k = k.contiguous()
+    npool = (-(-ph // kp)) * (-(-pw // kp))
+    pk = torch.empty(H, num_frames * npool, D, device=k.device, dtype=BF16)
+    pv = torch.empty_like(pk)
+    size = torch.empty(H, num_frames * npool, device=k.device, dtype=F32)
+    call("gpa_frame_pool", ptr(k), ptr(v), H, num_frames, ph, pw, num_special, kp, k.stride(0),
+         k.stride(1), ptr(pk), ptr(pv), pk.stride(0), pk.stride(1), ptr(size), stream_of(k))
+    return pk, pv, size
+
+
+def lse_combine(oa, la, ob, lb, out=None):
+    """Combine two partitions given as [H, S, P, D] (o*) and [H, S, P] (l*) views."""
+    require_cuda(oa, la, ob, lb, what="lse_combine")
+    H, S, P, D = oa.shape
+    if out is None:
+        out = torch.empty(H, S, P, D, device=oa.device, dtype=BF16)
+    A = _lib.i64array
+    call("gpa_lse_combine", H, S, P, D, ptr(oa), A(oa.stride()[:3]), ptr(la), A(la.stride()),
+         ptr(ob), A(ob.stride()[:3]), ptr(lb), A(lb.stride()), ptr(out), A(out.stride()[:3]),
+         stream_of(oa))
+    return out

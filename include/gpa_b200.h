@@ -1,0 +1,198 @@
+/*
+ * gpa_b200.h -- C ABI of the B200 (sm_100a) kernels for GPA-VGGT's accelerated
+ * global-attention path: bipartite K/V token merging (matching, plan,
+ * scatter-mean), log(count)-biased flash attention, and the frame attention
+ * with a shared cross-frame K/V set of the early global blocks.
+ *
+ * Conventions (all entry points):
+ *   - Plain device pointers, element strides (not bytes), sizes as int.
+ *     The innermost dimension of every tensor is contiguous.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).
+ *   - Outputs are caller-allocated; nothing here allocates device memory except
+ *     where a function says so.
+ *   - Return value: GPA_OK or an error code; gpa_last_error() gives the message
+ *     of the last failing call on this host thread.
+ *   - `status` (optional, may be NULL) is a device int that a kernel sets to a
+ *     nonzero code when one of its pipeline waits gave up (lost signal); the
+ *     kernel then returns early instead of hanging.  The caller reads it back.
+ *
+ * Reference interfaces replaced (paths inside noheat61/GPA-VGGT):
+ *   merging/fused_similarity.py:81-112   fused_similarity_argmax
+ *   merging/merge.py:87-176               dst/src split of token_merge_bipartite2d
+ *   merging/merge.py:180-187              projected metric normalise + split
+ *   merging/merge.py:189-217              edge ranking, dst_idx, merged_size
+ *   merging/merge.py:234-250              merge.heads (scatter-mean)
+ *   merging/fused_attention.py:130-180    attention_keybias
+ *   vggt/layers/attention.py:113-140      _pool (content-adaptive summaries)
+ *   vggt/layers/attention.py:164-176      two-partition log-sum-exp combine
+ */
+#ifndef GPA_B200_H
+#define GPA_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GPA_API __attribute__((visibility("default")))
+#else
+#define GPA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GPA_OK 0
+#define GPA_ERR_INVALID 1     /* bad argument: shape, stride, alignment, dtype */
+#define GPA_ERR_CUDA 2        /* CUDA runtime/driver error (launch, tensor map) */
+#define GPA_ERR_UNSUPPORTED 3 /* shape outside what the kernels implement */
+
+#define GPA_DTYPE_F32 0
+#define GPA_DTYPE_BF16 1
+
+/* Library version (major*10000 + minor*100 + patch). */
+GPA_API int gpa_version(void);
+
+/* Message of the last failing call on this host thread ("" if none). */
+GPA_API const char* gpa_last_error(void);
+
+/* Number of kernels this library has launched in this process so far. */
+GPA_API int64_t gpa_launch_count(void);
+
+/*
+ * Similarity + row argmax (replaces merging/fused_similarity.py:81-112, kernel
+ * _sim_argmax_kernel :33-78).  For each batch b and row i of a:
+ *   node_max[b,i] = max_j  sum_k a[b,i,k]*b[b,j,k]   (bf16 inputs, fp32 accumulate)
+ *   node_idx[b,i] = the smallest j attaining that max
+ * a: [batch, m, d] bf16, b: [batch, n, d] bf16; d % 64 == 0, 64 <= d <= 256.
+ * Row strides must be multiples of 8 elements, base pointers 16-byte aligned.
+ * node_max: [batch, m] fp32 contiguous; node_idx: [batch, m] int32 contiguous.
+ */
+GPA_API int gpa_sim_argmax(const void* a, const void* b, int batch, int m, int n, int d,
+                   int64_t a_stride_b, int64_t a_stride_m, int64_t b_stride_b,
+                   int64_t b_stride_n, float* node_max, int32_t* node_idx, int* status,
+                   void* stream);
+
+/*
+ * dst/src split of the multi-frame token sequence (replaces merging/merge.py:87-176).
+ * Tokens per frame P = w*h + num_special; num_imgs frames.  dst tokens: every
+ * token of frame 0, the num_special leading tokens of every frame, and one
+ * token per (sy x sx) window chosen by rand_idx[f-1, wy, wx] in [0, sx*sy)
+ * (rand_idx: device int64 [num_imgs-1, h/sy, w/sx], the values the reference
+ * draws with torch.randint; ignored when no_rand != 0).  As in the reference,
+ * the window pattern covers the first (h/sy*sy)*(w/sx*sx) patch positions of
+ * a frame taken contiguously.
+ * Outputs (device int32): dst_pos[num_dst], src_pos[num_src] -- absolute token
+ * positions in ascending order -- and slot[N]: the dst ordinal of a dst token,
+ * or -(src ordinal)-1 of a src token.  num_dst/num_src are given by
+ * gpa_merge_counts().
+ */
+GPA_API int gpa_merge_counts(int num_imgs, int w, int h, int sx, int sy, int num_special, int no_rand,
+                     int* num_dst, int* num_src);
+GPA_API int gpa_merge_roles(const int64_t* rand_idx, int num_imgs, int w, int h, int sx, int sy,
+                    int num_special, int no_rand, int32_t* dst_pos, int32_t* src_pos,
+                    int32_t* slot, void* stream);
+
+/*
+ * Normalise the projected matching metric and split it (replaces
+ * merging/merge.py:185-187 after the `metric @ proj` GEMM):
+ *   a[i] = bf16(metric[src_pos[i]] / ||metric[src_pos[i]]||)  (fp32 norm)
+ *   b[j] = bf16(metric[dst_pos[j]] / ||metric[dst_pos[j]]||)
+ * metric: [N, d], dtype GPA_DTYPE_BF16 or GPA_DTYPE_F32, row stride metric_stride;
+ * a: [num_src, d], b: [num_dst, d] contiguous bf16.  d % 8 == 0, d <= 1024.
+ */
+GPA_API int gpa_metric_split(const void* metric, int dtype, int64_t metric_stride, int d, const int32_t* src_pos,
+                     int num_src, const int32_t* dst_pos, int num_dst, void* a, void* b,
+                     void* stream);
+
+/*
+ * Merge plan (replaces merging/merge.py:189-217).  Given node_max/node_idx of
+ * the num_src src tokens, the r = min(r, num_src) src tokens with the largest
+ * node_max are merged into their matched dst; ties at the cut are broken by
+ * the lower src ordinal (a stable descending sort).  Outputs (device):
+ *   unm_src[num_src - r]   unmerged src ordinals, ascending (output slots 0..)
+ *   seg_start[num_dst + 1] CSR offsets into seg_src, per dst ordinal
+ *   seg_src[r]             merged src ordinals grouped by dst, ascending in a group
+ *   counts[N_m]            tokens behind each output slot (fp32):
+ *                          1 for unmerged src, 1 + group size for dst
+ * N_m = (num_src - r) + num_dst.  workspace: gpa_merge_plan_workspace_bytes().
+ */
+GPA_API int64_t gpa_merge_plan_workspace_bytes(int num_src, int num_dst);
+GPA_API int gpa_merge_plan(const float* node_max, const int32_t* node_idx, int num_src, int num_dst,
+                   int r, int32_t* unm_src, int32_t* seg_start, int32_t* seg_src,
+                   float* counts, void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
+ * Scatter-mean of one K or V tensor through a merge plan (replaces
+ * merging/merge.py:234-250, merge.heads(t, mode), and merge() at :222-232):
+ *   out[h, s]            = t[h, src_pos[unm_src[s]]]                 s < unm_len
+ *   out[h, unm_len + j]  = (t[h, dst_pos[j]] + sum_{i in seg j} t[h, src_pos[i]])
+ *                          / (1 + |seg j|)        (reduce_mean != 0, "mean")
+ *                          or without the division (reduce_mean == 0, "sum")
+ * t: [heads, n_tokens, head_dim] with strides (t_stride_h, t_stride_n), dtype
+ * GPA_DTYPE_F32 or GPA_DTYPE_BF16; out has the same dtype, [heads, N_m, head_dim]
+ * with strides (out_stride_h, out_stride_n).  Sums are fp32 in a fixed order
+ * (dst first, then src ordinal ascending), so the result is deterministic.
+ * head_dim % 8 == 0.  If log_counts != NULL, log of the tokens behind each slot
+ * (fp32 [N_m]) is also written there.
+ */
+GPA_API int gpa_merge_kv_mean(const void* t, int dtype, int heads, int n_tokens, int head_dim,
+                      int64_t t_stride_h, int64_t t_stride_n, const int32_t* src_pos,
+                      const int32_t* dst_pos, const int32_t* unm_src, int unm_len,
+                      const int32_t* seg_start, const int32_t* seg_src, int num_dst,
+                      int reduce_mean, float* log_counts, void* out, int64_t out_stride_h,
+                      int64_t out_stride_n, void* stream);
+
+/*
+ * Flash attention with a per-key additive bias (replaces
+ * merging/fused_attention.py:130-180, kernel _attn_keybias_kernel :70-127):
+ *   o[b,h,i]   = sum_j softmax_j(q.k_j * sm_scale + bias[b,h,j]) v_j
+ *   lse[b,h,i] = log2 of the softmax denominator in the exp2 domain
+ *                (m + log2(l) with scores scaled by log2(e)), as the reference.
+ * q: [batch, heads, m, 64], k/v: [batch, heads, n, 64], o: like q; all bf16,
+ * innermost dim contiguous, other strides multiples of 8 elements, 16-byte
+ * aligned bases.  bias: fp32 (natural-log domain), bias[b,h,j] at
+ * bias + b*bias_sb + h*bias_sh + j, or NULL for no bias.  lse may be NULL.
+ */
+GPA_API int gpa_attention_keybias(const void* q, const void* k, const void* v, const float* bias,
+                          int batch, int heads, int m, int n, int head_dim, int64_t q_sb,
+                          int64_t q_sh, int64_t q_sm, int64_t k_sb, int64_t k_sh, int64_t k_sn,
+                          int64_t v_sb, int64_t v_sh, int64_t v_sn, int64_t bias_sb,
+                          int64_t bias_sh, float sm_scale, void* o, int64_t o_sb, int64_t o_sh,
+                          int64_t o_sm, float* lse, int64_t lse_sb, int64_t lse_sh, int* status,
+                          void* stream);
+
+/*
+ * Content-adaptive pooling of each frame's patch keys/values (replaces
+ * vggt/layers/attention.py:113-140, _pool).  Per head hh and frame s the patch
+ * tokens t = num_special.. of k (grid ph x pw) join the seed on the stride-kp
+ * lattice with the highest cosine similarity (fp32, norms clamped at 1e-6,
+ * first seed on ties); a summary is the fp32 mean of its group.
+ * k, v: [heads, S*P, 64] bf16 with strides (stride_h, stride_n), P = ph*pw+num_special.
+ * Outputs: pk, pv [heads, S*npool, 64] bf16 with strides (out_stride_h, out_stride_n),
+ * pool_size [heads, S*npool] fp32 contiguous (group sizes), npool =
+ * ceil(ph/kp)*ceil(pw/kp) <= 64.
+ */
+GPA_API int gpa_frame_pool(const void* k, const void* v, int heads, int num_frames, int ph, int pw,
+                   int num_special, int kp, int64_t stride_h, int64_t stride_n, void* pk,
+                   void* pv, int64_t out_stride_h, int64_t out_stride_n, float* pool_size,
+                   void* stream);
+
+/*
+ * Exact combine of two attention partitions (replaces
+ * vggt/layers/attention.py:164-176): with log2 sums la, lb,
+ *   wa = 2^(la-mx), wb = 2^(lb-mx), mx = max(la, lb)
+ *   o  = bf16(wa/(wa+wb)) * oa + bf16(wb/(wa+wb)) * ob
+ * Rows are addressed as (head, frame, row-in-frame); each *_strides array holds
+ * the three element strides of that tensor in this order.  oa, ob, o: bf16
+ * with head_dim contiguous elements per row; la, lb: fp32.
+ */
+GPA_API int gpa_lse_combine(int heads, int frames, int rows_per_frame, int head_dim, const void* oa,
+                    const int64_t* oa_strides, const float* la, const int64_t* la_strides,
+                    const void* ob, const int64_t* ob_strides, const float* lb,
+                    const int64_t* lb_strides, void* o, const int64_t* o_strides, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GPA_B200_H */
