@@ -5,18 +5,27 @@
 // attention_keybias): o = softmax(q k^T * scale + bias) v with an online
 // softmax in the exp2 domain; optional log2 row sums lse = m + log2(l).
 //
-// B200 design (one CTA = two 128-query tiles of one (batch, head)):
+// B200 design (one CTA = two 128-query tiles of one (batch, head); 384 threads):
 //   warp 0      TMA producer: Q tiles once, then K/V tiles through a 3-stage
-//               ring; also stages the tile's bias row (x log2 e, -inf past n).
-//   warp 1      one thread issues tcgen05.mma: S_t = Q_t K^T into TMEM and
-//               O_t += P_t V into TMEM, ping-ponging the two query tiles so the
-//               tensor core works on one tile while the other is in softmax.
-//   warps 2-9   two softmax warpgroups (one per query tile; thread == row):
-//               read S from TMEM, online softmax with lazy rescaling (the
-//               running max is only moved when it grows by more than 2^8),
-//               write P as bf16 into 128B-swizzled shared memory (the layout
-//               the MMA reads), rescale O in TMEM when the max moved, and
-//               finally normalise O and store it.
+//               ring; stages each tile's bias row (x log2 e, -inf past n).
+//   warp 1      one thread issues tcgen05.mma: S_t = Q_t K^T (A and B from
+//               shared memory) and O_t += P_t V (P_t from TMEM, V from shared
+//               memory), ping-ponging the two query tiles so the tensor core
+//               works on one tile while the other is in softmax.
+//   warps 4-11  two softmax warpgroups, one per query tile, thread == row:
+//               S from TMEM -> online softmax -> P (bf16) back into TMEM.
+//               The running max only moves when it grows by more than 2^8
+//               (lazy rescale of O in TMEM); 3/8 of the exponentials run as a
+//               polynomial on the FMA pipe to offload the MUFU unit (16/clk/SM);
+//               scale/bias, max and sum use packed fp32x2 and 3-input max with
+//               independent accumulators.
+//   MMA order:  S_t(j+1) is issued as soon as softmax t has pulled S_t(j) into
+//               registers, before O_t += P_t(j) V_j, so a softmax warpgroup finds
+//               its next score tile ready when it finishes the current one.
+//   TMEM (512 columns): S0 0..127, S1 128..255, O0 256..319, O1 320..383,
+//                       P0 384..447, P1 448..511 (P: two bf16 per column).
+//   The producer/MMA warpgroup gives registers to the softmax warpgroups
+//   (setmaxnreg 56 / 216).
 #include "common.cuh"
 #include "capi_util.h"
 
@@ -28,22 +37,21 @@ constexpr int BN = 128;   // keys per tile
 constexpr int HD = 64;    // head dim
 constexpr int STAGES = 3;
 constexpr int TILE_BYTES = BM * HD * 2;  // 16 KB
-constexpr int P_BYTES = BM * BN * 2;     // 32 KB (two 16 KB swizzled chunks)
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+constexpr int THREADS = 384;
+constexpr int TMEM_COLS = 512;
+constexpr int REGS_LOW = 56, REGS_HIGH = 216, REGS_LAUNCH = 168;
+static_assert(REGS_LOW * 128 + REGS_HIGH * 256 <= REGS_LAUNCH * THREADS, "register split");
 
 struct Smem {
   static constexpr int Q = 0;                               // 2 x 16 KB
   static constexpr int K = Q + 2 * TILE_BYTES;              // STAGES x 16 KB
   static constexpr int V = K + STAGES * TILE_BYTES;         // STAGES x 16 KB
-  static constexpr int P = V + STAGES * TILE_BYTES;         // 2 x 32 KB
-  static constexpr int BIAS = P + 2 * P_BYTES;              // STAGES x 512 B
+  static constexpr int BIAS = V + STAGES * TILE_BYTES;      // STAGES x 512 B
   static constexpr int BARS = BIAS + STAGES * BN * 4;
   static constexpr int TOTAL = BARS + 256;
   static constexpr int ALLOC = TOTAL + 1024;
 };
-
-constexpr int THREADS = 320;
-constexpr int TMEM_COLS = 512;  // S0 0..127, S1 128..255, O0 256..319, O1 320..383
 
 struct Params {
   int m, n, heads;
@@ -57,7 +65,15 @@ struct Params {
   int* status;
 };
 
-__global__ void __launch_bounds__(THREADS)
+// exponentials of one group of 8 shifted scores: elements 5..7 on the FMA pipe
+__device__ __forceinline__ void exp8(const float* x, float* e) {
+#pragma unroll
+  for (int i = 0; i < 5; ++i) e[i] = fast_exp2(x[i]);
+  exp2_poly2(x[5], x[6], e[5], e[6]);
+  e[7] = exp2_poly(x[7]);
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
     attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                 const __grid_constant__ CUtensorMap map_v, const Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -104,116 +120,120 @@ __global__ void __launch_bounds__(THREADS)
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------ producer ------------------------------
-    const float* brow = p.bias ? p.bias + (int64_t)b * p.bias_sb + (int64_t)h * p.bias_sh : nullptr;
-    int issued = 0;
-    if (lane == 0) {
-      tma_prefetch_desc(&map_q);
-      tma_prefetch_desc(&map_k);
-      tma_prefetch_desc(&map_v);
-      bar_expect_tx(q_full, 2 * TILE_BYTES);
-      tma_load_4d(&map_q, q_full, smem + Smem::Q, 0, q0, h, b);
-      tma_load_4d(&map_q, q_full, smem + Smem::Q + TILE_BYTES, 0, q0 + BM, h, b);
-    }
-    for (int j = 0; j < nk; ++j) {
-      const int s = j % STAGES;
-      const uint32_t ph = (j / STAGES) & 1;
-      bool okw = wait_bar(&kv_empty[s], ph ^ 1, abort_flag, p.status, kDevTimeout);
-      if (!__all_sync(0xffffffffu, okw)) break;
-      float* bt = sbias + s * BN;
-#pragma unroll
-      for (int i = 0; i < BN / 32; ++i) {
-        const int c = i * 32 + lane;
-        const int col = j * BN + c;
-        float v = -INFINITY;
-        if (col < p.n) v = brow ? brow[col] * 1.4426950408889634f : 0.0f;
-        bt[c] = v;
-      }
-      __syncwarp();
+  if (warp < 4) {
+    regs_dec<REGS_LOW>();
+    if (warp == 0) {
+      // ------------------------------ producer ------------------------------
+      const float* brow = p.bias ? p.bias + (int64_t)b * p.bias_sb + (int64_t)h * p.bias_sh : nullptr;
+      int issued = 0;
       if (lane == 0) {
-        bar_expect_tx(&kv_full[s], 2 * TILE_BYTES);
-        tma_load_4d(&map_k, &kv_full[s], smem + Smem::K + s * TILE_BYTES, 0, j * BN, h, b);
-        tma_load_4d(&map_v, &kv_full[s], smem + Smem::V + s * TILE_BYTES, 0, j * BN, h, b);
+        tma_prefetch_desc(&map_q);
+        tma_prefetch_desc(&map_k);
+        tma_prefetch_desc(&map_v);
+        bar_expect_tx(q_full, 2 * TILE_BYTES);
+        tma_load_4d(&map_q, q_full, smem + Smem::Q, 0, q0, h, b);
+        tma_load_4d(&map_q, q_full, smem + Smem::Q + TILE_BYTES, 0, q0 + BM, h, b);
       }
-      issued = j + 1;
-    }
-    if (lane == 0) {  // drain copies in flight before the CTA can exit
-      const unsigned long long t0 = global_ns();
-      drain_bar(q_full, 0, t0);
-      for (int j = max(0, issued - STAGES); j < issued; ++j)
-        drain_bar(&kv_full[j % STAGES], (j / STAGES) & 1, t0);
-    }
-  } else if (warp == 1) {
-    // ------------------------------ MMA issuer ------------------------------
-    if (elect_one()) {
-      constexpr uint32_t idesc_s = idesc_bf16(BM, BN, false, false);
-      constexpr uint32_t idesc_o = idesc_bf16(BM, HD, false, true);
-      const uint32_t sQ = smem_u32(smem + Smem::Q);
-      const uint32_t sK = smem_u32(smem + Smem::K);
-      const uint32_t sV = smem_u32(smem + Smem::V);
-      const uint32_t sP = smem_u32(smem + Smem::P);
-      auto issue_s = [&](int t, int j) {
-        const uint32_t kaddr = sK + (j % STAGES) * TILE_BYTES;
-        const uint32_t qaddr = sQ + t * TILE_BYTES;
+      // bias of the next tile is fetched into registers one tile ahead
+      float bnext[BN / 32];
+      auto fetch_bias = [&](int j) {
 #pragma unroll
-        for (int k = 0; k < HD / 16; ++k)
-          umma_bf16(tbase + t * BN, sdesc_sw128(qaddr + k * 32, 16, 1024),
-                    sdesc_sw128(kaddr + k * 32, 16, 1024), idesc_s, k != 0);
-        umma_commit(&s_full[t]);
-      };
-      auto issue_o = [&](int t, int j) {
-        const uint32_t vaddr = sV + (j % STAGES) * TILE_BYTES;
-        const uint32_t paddr = sP + t * P_BYTES;
-#pragma unroll
-        for (int ks = 0; ks < BN / 16; ++ks)
-          umma_bf16(tbase + 256 + t * HD,
-                    sdesc_sw128(paddr + (ks >> 2) * TILE_BYTES + (ks & 3) * 32, 16, 1024),
-                    sdesc_sw128(vaddr + ks * 2048, 16384, 1024), idesc_o, (j > 0 || ks > 0));
-        umma_commit(&o_done[t]);
-      };
-      bool okw = wait_bar(q_full, 0, abort_flag, p.status, kDevTimeout) &&
-                 wait_bar(&kv_full[0], 0, abort_flag, p.status, kDevTimeout);
-      if (okw) {
-        tc_fence_after();
-        issue_s(0, 0);
-        issue_s(1, 0);
-      }
-      for (int j = 0; okw && j < nk; ++j) {
-        const bool more = j + 1 < nk;
-        // O0 += P0 V_j ; then S0 for the next tile
-        if (!(okw = wait_bar(&p_full[0], j & 1, abort_flag, p.status, kDevTimeout))) break;
-        tc_fence_after();
-        issue_o(0, j);
-        if (more) {
-          if (!(okw = wait_bar(&kv_full[(j + 1) % STAGES], ((j + 1) / STAGES) & 1, abort_flag,
-                               p.status, kDevTimeout)))
-            break;
-          if (!(okw = wait_bar(&s_empty[0], j & 1, abort_flag, p.status, kDevTimeout))) break;
-          tc_fence_after();
-          issue_s(0, j + 1);
+        for (int i = 0; i < BN / 32; ++i) {
+          const int col = j * BN + i * 32 + lane;
+          bnext[i] = col < p.n ? (brow ? __ldg(brow + col) * 1.4426950408889634f : 0.0f) : -INFINITY;
         }
-        // O1 += P1 V_j ; release the K/V stage ; then S1 for the next tile
-        if (!(okw = wait_bar(&p_full[1], j & 1, abort_flag, p.status, kDevTimeout))) break;
-        tc_fence_after();
-        issue_o(1, j);
-        umma_commit(&kv_empty[j % STAGES]);
-        if (more) {
-          if (!(okw = wait_bar(&s_empty[1], j & 1, abort_flag, p.status, kDevTimeout))) break;
+      };
+      fetch_bias(0);
+      for (int j = 0; j < nk; ++j) {
+        const int s = j % STAGES;
+        const uint32_t ph = (j / STAGES) & 1;
+        bool okw = wait_bar(&kv_empty[s], ph ^ 1, abort_flag, p.status, kDevTimeout);
+        if (!__all_sync(0xffffffffu, okw)) break;
+        float* bt = sbias + s * BN;
+#pragma unroll
+        for (int i = 0; i < BN / 32; ++i) bt[i * 32 + lane] = bnext[i];
+        __syncwarp();
+        if (lane == 0) {
+          bar_expect_tx(&kv_full[s], 2 * TILE_BYTES);
+          tma_load_4d(&map_k, &kv_full[s], smem + Smem::K + s * TILE_BYTES, 0, j * BN, h, b);
+          tma_load_4d(&map_v, &kv_full[s], smem + Smem::V + s * TILE_BYTES, 0, j * BN, h, b);
+        }
+        issued = j + 1;
+        if (j + 1 < nk) fetch_bias(j + 1);
+      }
+      if (lane == 0) {  // drain copies in flight before the CTA can exit
+        const unsigned long long t0 = global_ns();
+        drain_bar(q_full, 0, t0);
+        for (int j = max(0, issued - STAGES); j < issued; ++j)
+          drain_bar(&kv_full[j % STAGES], (j / STAGES) & 1, t0);
+      }
+    } else if (warp == 1) {
+      // ------------------------------ MMA issuer ------------------------------
+      if (elect_one()) {
+        constexpr uint32_t idesc_s = idesc_bf16(BM, BN, false, false);
+        constexpr uint32_t idesc_o = idesc_bf16(BM, HD, false, true);
+        const uint32_t sQ = smem_u32(smem + Smem::Q);
+        const uint32_t sK = smem_u32(smem + Smem::K);
+        const uint32_t sV = smem_u32(smem + Smem::V);
+        auto issue_s = [&](int t, int j) {
+          const uint32_t kaddr = sK + (j % STAGES) * TILE_BYTES;
+          const uint32_t qaddr = sQ + t * TILE_BYTES;
+#pragma unroll
+          for (int k = 0; k < HD / 16; ++k)
+            umma_bf16(tbase + t * BN, sdesc_sw128(qaddr + k * 32, 16, 1024),
+                      sdesc_sw128(kaddr + k * 32, 16, 1024), idesc_s, k != 0);
+          umma_commit(&s_full[t]);
+        };
+        auto issue_o = [&](int t, int j) {
+          const uint32_t vaddr = sV + (j % STAGES) * TILE_BYTES;
+          const uint32_t ptm = tbase + 384 + t * 64;
+#pragma unroll
+          for (int ks = 0; ks < BN / 16; ++ks)
+            umma_bf16_ts(tbase + 256 + t * HD, ptm + ks * 8, sdesc_sw128(vaddr + ks * 2048, 16384, 1024),
+                         idesc_o, (j > 0 || ks > 0));
+          umma_commit(&o_done[t]);
+        };
+        bool okw = wait_bar(q_full, 0, abort_flag, p.status, kDevTimeout) &&
+                   wait_bar(&kv_full[0], 0, abort_flag, p.status, kDevTimeout);
+        if (okw) {
           tc_fence_after();
-          issue_s(1, j + 1);
+          issue_s(0, 0);
+          issue_s(1, 0);
+        }
+        for (int j = 0; okw && j < nk; ++j) {
+          if (j + 1 < nk) {  // next score tiles, as soon as the softmax holds S(j)
+            if (!(okw = wait_bar(&kv_full[(j + 1) % STAGES], ((j + 1) / STAGES) & 1, abort_flag,
+                                 p.status, kDevTimeout)))
+              break;
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              if (!(okw = wait_bar(&s_empty[t], j & 1, abort_flag, p.status, kDevTimeout))) break;
+              tc_fence_after();
+              issue_s(t, j + 1);
+            }
+            if (!okw) break;
+          }
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            if (!(okw = wait_bar(&p_full[t], j & 1, abort_flag, p.status, kDevTimeout))) break;
+            tc_fence_after();
+            issue_o(t, j);
+          }
+          if (!okw) break;
+          umma_commit(&kv_empty[j % STAGES]);
         }
       }
     }
   } else {
+    regs_inc<REGS_HIGH>();
     // ------------------------------ softmax ------------------------------
-    const int t = (warp - 2) >> 2;       // query tile of this warpgroup
+    const int t = (warp - 4) >> 2;       // query tile of this warpgroup
     const int quad = warp & 3;           // TMEM lane quadrant
     const int r = quad * 32 + lane;      // row within the tile
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const uint32_t tS = tbase + lane_off + t * BN;
     const uint32_t tO = tbase + lane_off + 256 + t * HD;
-    uint8_t* sP = smem + Smem::P + t * P_BYTES;
+    const uint32_t tP = tbase + lane_off + 384 + t * 64;
     float m_ref = -INFINITY, l = 0.f;
     bool okw = true;
     for (int j = 0; j < nk; ++j) {
@@ -231,16 +251,20 @@ __global__ void __launch_bounds__(THREADS)
       if (lane == 0) bar_arrive(&s_empty[t]);
 
       const float4* bt = reinterpret_cast<const float4*>(sbias + s * BN);
-      float mt = -INFINITY;
+      float mx[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) mx[i] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < BN / 4; ++c) {
-        float4 bb = bt[c];
-        x[4 * c + 0] = fmaf(x[4 * c + 0], p.scale_log2, bb.x);
-        x[4 * c + 1] = fmaf(x[4 * c + 1], p.scale_log2, bb.y);
-        x[4 * c + 2] = fmaf(x[4 * c + 2], p.scale_log2, bb.z);
-        x[4 * c + 3] = fmaf(x[4 * c + 3], p.scale_log2, bb.w);
-        mt = fmaxf(mt, fmaxf(fmaxf(x[4 * c], x[4 * c + 1]), fmaxf(x[4 * c + 2], x[4 * c + 3])));
+        const float4 bb = bt[c];
+        ffma2(x[4 * c + 0], x[4 * c + 1], x[4 * c + 0], x[4 * c + 1], p.scale_log2, p.scale_log2,
+              bb.x, bb.y);
+        ffma2(x[4 * c + 2], x[4 * c + 3], x[4 * c + 2], x[4 * c + 3], p.scale_log2, p.scale_log2,
+              bb.z, bb.w);
+        mx[c & 3] = fmax3(mx[c & 3], x[4 * c + 0], x[4 * c + 1]);
+        mx[c & 3] = fmax3(mx[c & 3], x[4 * c + 2], x[4 * c + 3]);
       }
+      const float mt = fmax3(fmaxf(mx[0], mx[1]), mx[2], mx[3]);
       float alpha = 1.f;
       const bool moved = mt > m_ref + kRescaleThreshold;
       if (moved) {
@@ -254,25 +278,28 @@ __global__ void __launch_bounds__(THREADS)
         if (!__all_sync(0xffffffffu, okw)) { okw = false; break; }
         tc_fence_after();
       }
-      // P row -> shared memory, 128B swizzle, K-major (chunk = 64 keys)
-      float rs = 0.f;
+      float acc[8];
 #pragma unroll
-      for (int u = 0; u < BN / 8; ++u) {
-        const int chunk = u >> 3, uu = u & 7;
-        float e[8];
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+      const float neg_m = -m_ref;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          e[i] = fast_exp2(x[8 * u + i] - m_ref);
-          rs += e[i];
+      for (int hf = 0; hf < 2; ++hf) {  // 64 keys -> 32 packed columns per half
+        uint32_t pk[32];
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          float* xg = x + hf * 64 + g * 8;
+#pragma unroll
+          for (int i = 0; i < 8; i += 2) fadd2(xg[i], xg[i + 1], xg[i], xg[i + 1], neg_m, neg_m);
+          float e[8];
+          exp8(xg, e);
+#pragma unroll
+          for (int i = 0; i < 8; i += 2) fadd2(acc[i], acc[i + 1], acc[i], acc[i + 1], e[i], e[i + 1]);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) pk[g * 4 + i] = pack_bf16x2(e[2 * i], e[2 * i + 1]);
         }
-        uint4 pk;
-        pk.x = pack_bf16x2(e[0], e[1]);
-        pk.y = pack_bf16x2(e[2], e[3]);
-        pk.z = pack_bf16x2(e[4], e[5]);
-        pk.w = pack_bf16x2(e[6], e[7]);
-        *reinterpret_cast<uint4*>(sP + chunk * TILE_BYTES + r * 128 + ((uu ^ (r & 7)) << 4)) = pk;
+        tmem_st32(tP + hf * 32, pk);
       }
-      l += rs;
+      l += ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
       // rescale O_t in TMEM where the running max moved
       if (j > 0 && __any_sync(0xffffffffu, moved)) {
         uint32_t ov[32];
@@ -282,12 +309,10 @@ __global__ void __launch_bounds__(THREADS)
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-          tmem_st16(tO + hf * 32, ov);
-          tmem_st16(tO + hf * 32 + 16, ov + 16);
+          tmem_st32(tO + hf * 32, ov);
         }
-        tmem_wait_st();
       }
-      fence_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) bar_arrive(&p_full[t]);
@@ -342,6 +367,25 @@ static int make_map4(CUtensorMap* map, const void* base, int n_rows, int heads, 
   return make_map_bf16(map, base, 4, dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B, what);
 }
 
+// The register split needs the kernel to be launched with REGS_LAUNCH
+// registers per thread; refuse to launch otherwise (it would never start).
+static int check_regs() {
+  static int checked = 0;
+  if (checked) return checked > 0 ? GPA_OK : GPA_ERR_CUDA;
+  cudaFuncAttributes fa;
+  if (cudaFuncGetAttributes(&fa, attn_kernel) != cudaSuccess) {
+    checked = -1;
+    return fail(GPA_ERR_CUDA, "gpa_attention_keybias: cudaFuncGetAttributes failed");
+  }
+  if (fa.numRegs * THREADS < REGS_LOW * 128 + REGS_HIGH * 256) {
+    checked = -1;
+    return fail(GPA_ERR_CUDA, "gpa_attention_keybias: kernel built with %d registers/thread, "
+                "the warpgroup register split needs %d", fa.numRegs, REGS_LAUNCH);
+  }
+  checked = 1;
+  return GPA_OK;
+}
+
 }  // namespace attn
 }  // namespace gpa
 
@@ -365,8 +409,10 @@ extern "C" int gpa_attention_keybias(const void* q, const void* k, const void* v
   if (m == 0) return ok();
   if ((int64_t)batch * heads > 65535)
     return fail(GPA_ERR_UNSUPPORTED, "gpa_attention_keybias: batch*heads > 65535");
+  int rc = check_regs();
+  if (rc) return rc;
   CUtensorMap mq, mk, mv;
-  int rc = make_map4(&mq, q, m, heads, batch, q_sm, q_sh, q_sb, "gpa_attention_keybias(q)");
+  rc = make_map4(&mq, q, m, heads, batch, q_sm, q_sh, q_sb, "gpa_attention_keybias(q)");
   if (!rc) rc = make_map4(&mk, k, n, heads, batch, k_sn, k_sh, k_sb, "gpa_attention_keybias(k)");
   if (!rc) rc = make_map4(&mv, v, n, heads, batch, v_sn, v_sh, v_sb, "gpa_attention_keybias(v)");
   if (rc) return rc;

@@ -6,6 +6,7 @@ launch on the current stream.  One function per entry point of
 from __future__ import annotations
 
 import ctypes
+import os
 from dataclasses import dataclass
 from typing import Optional
 
@@ -16,6 +17,27 @@ from ._lib import call, ptr, stream_of, require_cuda, aligned
 
 BF16 = torch.bfloat16
 F32 = torch.float32
+
+# GPA_CHECK_STATUS=1: every pipelined kernel gets a device status word that is
+# read back after the launch (synchronises); a nonzero status -- a pipeline
+# wait that gave up -- raises.  Off by default (no host sync on the hot path).
+CHECK_STATUS = os.environ.get("GPA_CHECK_STATUS", "0") == "1"
+
+
+class KernelTimeout(RuntimeError):
+    """A kernel's pipeline wait gave up (device status word set)."""
+
+
+def _status_word(status, device):
+    if status is None and CHECK_STATUS:
+        return torch.zeros(1, device=device, dtype=torch.int32), True
+    return status, False
+
+
+def _check_status(status, what):
+    v = int(status.item())
+    if v != 0:
+        raise KernelTimeout(f"{what}: device status {v} (a pipeline wait gave up)")
 
 
 def _dt(t: torch.Tensor) -> int:
@@ -46,8 +68,11 @@ def sim_argmax(a: torch.Tensor, b: torch.Tensor, status: Optional[torch.Tensor] 
     N = b.shape[1]
     node_max = torch.empty(B, M, device=a.device, dtype=F32)
     node_idx = torch.empty(B, M, device=a.device, dtype=torch.int32)
+    status, own = _status_word(status, a.device)
     call("gpa_sim_argmax", ptr(a), ptr(b), B, M, N, D, a.stride(0), a.stride(1), b.stride(0),
          b.stride(1), ptr(node_max), ptr(node_idx), ptr(status), stream_of(a))
+    if own:
+        _check_status(status, "gpa_sim_argmax")
     return node_max, node_idx
 
 
@@ -177,12 +202,15 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bias: Optional[
     if out is None:
         out = torch.empty(B, H, M, D, device=q.device, dtype=BF16)
     lse = torch.empty(B, H, M, device=q.device, dtype=F32) if return_lse else None
+    status, own = _status_word(status, q.device)
     call("gpa_attention_keybias", ptr(q), ptr(k), ptr(v), ptr(bias), B, H, M, N, D,
          q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
          v.stride(0), v.stride(1), v.stride(2), bsb, bsh, float(sm_scale), ptr(out),
          out.stride(0), out.stride(1), out.stride(2), ptr(lse),
          lse.stride(0) if lse is not None else 0, lse.stride(1) if lse is not None else 0,
          ptr(status), stream_of(q))
+    if own:
+        _check_status(status, "gpa_attention_keybias")
     return (out, lse) if return_lse else out
 
 

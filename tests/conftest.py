@@ -1,5 +1,9 @@
+import os
 import sys
 from pathlib import Path
+
+# every pipelined kernel launched by the tests reads back its status word
+os.environ.setdefault("GPA_CHECK_STATUS", "1")
 
 import pytest
 
