@@ -35,6 +35,7 @@ SIGNATURES = {
     "gpa_metric_split": (_c_int, [_vp, _c_int, _c_i64, _c_int, _vp, _c_int, _vp, _c_int, _vp, _vp, _vp]),
     "gpa_merge_plan_workspace_bytes": (_c_i64, [_c_int, _c_int]),
     "gpa_merge_plan": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _c_i64, _vp]),
+    "gpa_merge_plan_noalloc": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp]),
     "gpa_merge_kv_mean": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_i64, _c_i64, _vp, _vp, _vp,
                                    _c_int, _vp, _vp, _c_int, _c_int, _vp, _vp, _c_i64, _c_i64, _vp]),
     "gpa_attention_keybias": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,

@@ -668,3 +668,70 @@ extern "C" int gpa_merge_kv_mean(const void* t, int dtype, int heads, int n_toke
 #undef GPA_MERGE_LAUNCH
   return check_launch("gpa_merge_kv_mean");
 }
+
+// ===========================================================================
+// Merge plan without any device allocation.
+//
+// Some callers of this library cannot allocate device memory when they call
+// in: an inference server or plugin host that hands the whole GPU to its own
+// memory arena up front (a cudaMalloc there would bypass the arena, can fail
+// under memory pressure, and synchronises the device in the middle of
+// serving), or an FFI caller that owns no allocator at all.  For them the
+// plan's scratch lives in the fixed array below, which the library carries on
+// every GPU that loads it, until the process exits.
+//
+// * The first call on a device looks up the array's device address with
+//   cudaGetSymbolAddress (host code only sees a host-side stand-in under that
+//   name); make that first call before any stream capture on that device.
+// * Every call on a device shares the one array and leaves its last contents
+//   behind; the plan writes or clears every word it reads, so stale contents
+//   never leak into a result, but two calls that overlap on the GPU (other
+//   streams, other host threads) race on the array.
+// * Sizes whose scratch would not fit (gpa_merge_plan_workspace_bytes above
+//   GPA_NOALLOC_SCRATCH_BYTES: about 786k src with 262k dst tokens) are
+//   rejected with GPA_ERR_UNSUPPORTED before anything is launched.
+// ===========================================================================
+#include <mutex>
+
+namespace {
+static __device__ __align__(256) unsigned char g_plan_scratch[GPA_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {nullptr};
+
+int plan_scratch_for_current_device(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(GPA_ERR_CUDA, "gpa_merge_plan_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(GPA_ERR_UNSUPPORTED, "gpa_merge_plan_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_plan_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(GPA_ERR_CUDA, "gpa_merge_plan_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return GPA_OK;
+}
+}  // namespace
+
+extern "C" int gpa_merge_plan_noalloc(const float* node_max, const int32_t* node_idx, int num_src,
+                                      int num_dst, int r, int32_t* unm_src, int32_t* seg_start,
+                                      int32_t* seg_src, float* counts, void* stream) {
+  if (num_src < 0 || num_dst <= 0 || r < 0)
+    return fail(GPA_ERR_INVALID, "gpa_merge_plan_noalloc: bad sizes");
+  const int64_t need = gpa_merge_plan_workspace_bytes(num_src, num_dst);
+  if (need < 0 || need > (int64_t)GPA_NOALLOC_SCRATCH_BYTES)
+    return fail(GPA_ERR_UNSUPPORTED,
+                "gpa_merge_plan_noalloc: %d src / %d dst tokens need %lld scratch bytes, more than "
+                "the library's fixed %lld (use gpa_merge_plan with a workspace)",
+                num_src, num_dst, (long long)need, (long long)GPA_NOALLOC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  int rc = plan_scratch_for_current_device(&scratch);
+  if (rc) return rc;
+  return gpa_merge_plan(node_max, node_idx, num_src, num_dst, r, unm_src, seg_start, seg_src,
+                        counts, scratch, (int64_t)GPA_NOALLOC_SCRATCH_BYTES, stream);
+}

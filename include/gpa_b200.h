@@ -122,6 +122,23 @@ GPA_API int gpa_merge_plan(const float* node_max, const int32_t* node_idx, int n
                    float* counts, void* workspace, int64_t workspace_bytes, void* stream);
 
 /*
+ * Merge plan for callers that must not allocate device memory (no counterpart
+ * in the reference).  Same inputs, outputs and results as gpa_merge_plan, but
+ * the scratch is a fixed array of GPA_NOALLOC_SCRATCH_BYTES inside the library
+ * on each GPU (held until the process exits), so the call allocates nothing.
+ * Meant for hosts that give all device memory to their own arena up front, or
+ * FFI callers without an allocator.  The first call on a device resolves the
+ * array's address (make it before any stream capture); calls that overlap on
+ * the GPU race on the shared array; sizes whose scratch exceeds the array
+ * (gpa_merge_plan_workspace_bytes > GPA_NOALLOC_SCRATCH_BYTES, about 786k src
+ * with 262k dst tokens) return GPA_ERR_UNSUPPORTED without launching.
+ */
+#define GPA_NOALLOC_SCRATCH_BYTES (16u << 20)
+GPA_API int gpa_merge_plan_noalloc(const float* node_max, const int32_t* node_idx, int num_src,
+                                   int num_dst, int r, int32_t* unm_src, int32_t* seg_start,
+                                   int32_t* seg_src, float* counts, void* stream);
+
+/*
  * Scatter-mean of one K or V tensor through a merge plan (replaces
  * merging/merge.py:234-250, merge.heads(t, mode), and merge() at :222-232):
  *   out[h, s]            = t[h, src_pos[unm_src[s]]]                 s < unm_len
