@@ -1,27 +1,31 @@
-"""Benchmark of the GPA-VGGT accelerated attention path on B200.
+"""Benchmark: GPA-VGGT forward on B200 (the reference's bench_e2e workload).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--frames S] [--workload merged_block]
+                    [--frames S] [--workload forward|merged_block] [--vanilla]
 
-Workload "merged_block" (default): one GPA merged global block's attention
-core at S frames (default 200; 518x518 -> 37x37 patches + 5 special tokens
-per frame, dim 1024, 16 heads x 64): dst/src roles, 1024->128 random
-projection of the matching metric, similarity argmax, merge plan, K and V
-scatter-mean, log(count)-biased flash attention over all S*1374 queries.
-Inputs are resident in HBM when timing starts; they are larger than L2
-(qkv alone is 1.7 GB at S=200), so no flush is needed between steps.
+Workload "forward" (default): the full GPA-VGGT forward -- DINO patch embed,
+24 alternating frame/global blocks with the GPA schedule (9 frame+shared-set
+blocks, 11 merged blocks at ratio 0.98, 4 core blocks at 0.2), camera head and
+DPT depth head -- on S = 200 synthetic 518x518 frames (torch.rand, seed 0),
+random-init VGGT-1B weights (gpa_vggt_b200.vggt.init_weights, seed 0), model
+in bf16 under bf16 autocast, as eval/bench_e2e.py:90-95 of the reference.
+Every head_dim-64 attention (global, frame and DINO blocks) runs on the
+sm_100a kernels.  Inputs resident in HBM; the activations are far larger than
+L2, so no flush is needed between steps.
 
-With N > 1 (torchrun), each rank runs the same block on its own replica of
-the inputs (weak scaling, no collective on the data path).
+Workload "merged_block": one merged global block's attention core at S frames
+(roles, projection, similarity argmax, plan, K/V scatter-mean, biased
+attention).
 
-One JSON line is printed by rank 0.  --impl reference times the reference's
-CPU path (the oracle port in oracle/) on the host cores instead.
+With N > 1 (torchrun) each rank runs its own replica (weak scaling) until the
+query-frame sharding lands.  --impl reference times the reference's CPU path
+(the oracle port in oracle/, torch on all host cores) on a bounded sample and
+extrapolates it to the same workload.
 """
 from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 import subprocess
@@ -34,17 +38,19 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 P_TOK = 37 * 37 + 5  # tokens per frame
+METRIC = "GPA-VGGT fwd latency (ms) & frames/s at S=200, 1/2/4/8 B200; % roofline"
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--frames", type=int, default=200)
     ap.add_argument("--ratio", type=float, default=0.98)
-    ap.add_argument("--workload", default="merged_block", choices=["merged_block"])
+    ap.add_argument("--workload", default="forward", choices=["forward", "merged_block"])
+    ap.add_argument("--vanilla", action="store_true", help="no merging, no frame+shared set")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     return ap.parse_args()
@@ -75,8 +81,7 @@ class Clocks:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
+            threading.Thread(target=self._read, daemon=True).start()
         except OSError:
             self.proc = None
         return self
@@ -94,7 +99,7 @@ class Clocks:
                 self.proc.kill()
 
     def summary(self):
-        sm, mx, reasons = [], 0.0, set()
+        sm, mx, reasons, power = [], 0.0, set(), []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
             f = [x.strip() for x in ln.split(",")]
@@ -103,6 +108,7 @@ class Clocks:
             try:
                 sm.append(float(f[0]))
                 mx = max(mx, float(f[1]))
+                power.append(float(f[2]))
             except ValueError:
                 continue
             for n, v in zip(names, f[3:7]):
@@ -111,13 +117,32 @@ class Clocks:
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "power_w_max": max(power) if power else None, "samples": len(sm)}
 
 
 # ----------------------------------------------------------------------------
-# workload: one merged global block
+# workloads
 # ----------------------------------------------------------------------------
-def make_inputs(S, dev, seed=0):
+def build_model(dev, vanilla=False):
+    import torch
+    from gpa_vggt_b200.vggt import VGGT, init_weights, vanilla_config
+    m = VGGT(**(vanilla_config() if vanilla else {}))
+    init_weights(m, seed=0)
+    m = m.eval().to(dev).to(torch.bfloat16)
+    m.update_patch_dimensions(37, 37)
+    return m
+
+
+def forward(model, images):
+    import torch
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        taps, psi = model.aggregator(images)
+        pose = model.camera_head(taps)[-1]
+        depth, conf = model.depth_head(taps, images=images, patch_start_idx=psi)
+    return pose, depth, conf
+
+
+def make_block_inputs(S, dev, seed=0):
     import torch
     g = torch.Generator(device="cpu").manual_seed(seed)
     N = S * P_TOK
@@ -126,10 +151,9 @@ def make_inputs(S, dev, seed=0):
     return x.to(dev), qkv.to(dev)
 
 
-def merged_block(x, qkv, ratio, out=None, timers=None):
-    """The hot path of one merged block (attention.py:233-268) on device
-    tensors: x [N, 1024] (norm1 output = matching metric), qkv [N, 3, 16, 64]
-    -> attention output [N, 16, 64]."""
+def merged_block(x, qkv, ratio, out=None):
+    """One merged block's attention core (attention.py:233-268) on device
+    tensors: x [N, 1024] (matching metric), qkv [N, 3, 16, 64] -> [N, 16, 64]."""
     import torch
     from gpa_vggt_b200 import kernels
     from gpa_vggt_b200.merging.merge import build_plan
@@ -137,81 +161,114 @@ def merged_block(x, qkv, ratio, out=None, timers=None):
     gen = torch.Generator(device=x.device)
     gen.manual_seed(33)
     plan = build_plan(x, 37, 37, 2, 2, int(N * ratio), False, gen, 128, 5)
-    k = qkv[:, 1].transpose(0, 1)  # [H, N, D] views
-    v = qkv[:, 2].transpose(0, 1)
     km = torch.empty(plan.n_out, 16, 64, device=x.device, dtype=torch.bfloat16)
     vm = torch.empty_like(km)
     logc = torch.empty(plan.n_out, device=x.device, dtype=torch.float32)
-    kernels.merge_kv(k, plan, out=km.transpose(0, 1), log_counts=logc)
-    kernels.merge_kv(v, plan, out=vm.transpose(0, 1))
-    q = qkv[:, 0].transpose(0, 1)[None]
+    kernels.merge_kv(qkv[:, 1].transpose(0, 1), plan, out=km.transpose(0, 1), log_counts=logc)
+    kernels.merge_kv(qkv[:, 2].transpose(0, 1), plan, out=vm.transpose(0, 1))
     if out is None:
         out = torch.empty(N, 16, 64, device=x.device, dtype=torch.bfloat16)
-    if timers is not None:
-        timers[0].record()
-    kernels.attention(q, km.transpose(0, 1)[None], vm.transpose(0, 1)[None], logc[None, None],
-                      64 ** -0.5, out=out.transpose(0, 1)[None])
-    if timers is not None:
-        timers[1].record()
+    kernels.attention(qkv[:, 0].transpose(0, 1)[None], km.transpose(0, 1)[None],
+                      vm.transpose(0, 1)[None], logc[None, None], 64 ** -0.5,
+                      out=out.transpose(0, 1)[None])
     return out, plan
 
 
-def attn_flops(S, n_m):
-    return 4.0 * S * P_TOK * n_m * 64 * 16
+# ----------------------------------------------------------------------------
+# CPU baseline: the reference path on the host cores, composed from samples
+# ----------------------------------------------------------------------------
+def _t(fn, reps=1):
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        fn()
+    return (time.perf_counter() - t0) / reps
 
 
-# ----------------------------------------------------------------------------
-# CPU baseline: the oracle port on a bounded sample
-# ----------------------------------------------------------------------------
-def cpu_block_ms(S, ratio, budget_s=20.0):
-    """ms for one merged block on the host cores, extrapolated from a sample:
-    all of the matching (roles, projection, normalise) at full size, the
-    similarity argmax and the attention on a subset of rows, scaled by the
-    subset fraction."""
+def merged_len(S, ratio):
+    nd = P_TOK + (S - 1) * 329
+    ns = S * P_TOK - nd
+    r = int(S * P_TOK * ratio)
+    return nd if r >= ns else ns - r + nd
+
+
+def cpu_block_parts(S):
+    """Seconds on the host cores (torch CPU fp32, all threads) for the pieces of
+    one GPA forward at S frames, each measured on a bounded sample and scaled by
+    the fraction of rows / frames it covers."""
     import torch
+    import torch.nn.functional as F
     from oracle import gpa_oracle as O
     torch.set_num_threads(os.cpu_count() or 1)
     g = torch.Generator().manual_seed(0)
     N = S * P_TOK
-    nd = P_TOK + (S - 1) * 329
-    ns = N - nd
-    n_m = nd if int(N * ratio) >= ns else ns - int(N * ratio) + nd
-    x = torch.randn(N, 1024, generator=g)
-    t0 = time.perf_counter()
-    rand = torch.randint(4, (S - 1, 18, 18), generator=g)
-    mask = O.dst_mask(S, 37, 37, 2, 2, 5, rand)
-    dst, src = O.split_positions(mask)
-    proj = torch.randn(1024, 128, generator=g)
-    mn = O.normalize_rows(x @ proj)
-    t_match = time.perf_counter() - t0
-    # similarity on a row subset (fp32 GEMM + max, the reference's chunked matcher shape)
-    sub = max(64, min(ns, int(ns / 64)))
-    a, b = mn[src[:sub]], mn[dst]
-    t0 = time.perf_counter()
-    s = a @ b.T
-    s.max(dim=1)
-    t_sim = (time.perf_counter() - t0) * ns / sub
-    # merge: gathers + index_add over all rows of K and V (fp32, [N, 1024])
-    kv = torch.randn(N, 1024, generator=g)
-    t0 = time.perf_counter()
-    idx = torch.randint(0, nd, (ns,), generator=g)
-    for _ in range(2):
-        mid = kv[dst].clone()
-        mid.index_add_(0, idx, kv[src])
-    t_merge = time.perf_counter() - t0
-    # attention on a query subset: fp32 SDPA with a bias over all merged keys
-    qs = max(128, min(N, int(N / 512)))
+    parts = {}
+    # linear layers of one block (qkv, proj, fc1, fc2) on 1024 rows
+    R = 1024
+    xr = torch.randn(R, 1024, generator=g)
+    w = [torch.randn(o, i, generator=g) * 0.02 for o, i in ((3072, 1024), (1024, 1024), (4096, 1024), (1024, 4096))]
+    def lin():
+        F.linear(xr, w[0]); F.linear(xr, w[1]); h = F.linear(xr, w[2]); F.linear(h, w[3])
+    parts["linear_per_block"] = _t(lin, 2) * N / R
+    # per-frame attention (frame blocks, DINO blocks, own-frame part of early blocks)
+    qf = torch.randn(1, 16, P_TOK, 64, generator=g)
+    parts["frame_attn_per_block"] = _t(lambda: F.scaled_dot_product_attention(qf, qf, qf), 2) * S
+    # shared-set attention of an early block on a query sample
+    qs = 2048
     q = torch.randn(1, 16, qs, 64, generator=g)
-    k = torch.randn(1, 16, n_m, 64, generator=g)
-    v = torch.randn(1, 16, n_m, 64, generator=g)
-    bias = torch.rand(1, 1, 1, n_m, generator=g)
+    ksh = torch.randn(1, 16, 30 * S, 64, generator=g)
+    parts["shared_attn_per_block"] = _t(lambda: F.scaled_dot_product_attention(q, ksh, ksh,
+                                        attn_mask=torch.zeros(1, 1, 1, 30 * S)), 1) * N / qs
+    # merged-block matching (roles, projection, normalise) at full size, similarity on a sample
+    x = torch.randn(N, 1024, generator=g)
+    def match():
+        rand = torch.randint(4, (S - 1, 18, 18), generator=g)
+        mask = O.dst_mask(S, 37, 37, 2, 2, 5, rand)
+        d, s_ = O.split_positions(mask)
+        mn = O.normalize_rows(x @ torch.randn(1024, 128, generator=g))
+        return mn, d, s_
     t0 = time.perf_counter()
-    torch.nn.functional.scaled_dot_product_attention(q, k, v, attn_mask=bias)
-    t_attn = (time.perf_counter() - t0) * N / qs
-    total = t_match + t_sim + t_merge + t_attn
-    sample = (f"one merged block at S={S}: matching + merge at full size, similarity on "
-              f"{sub}/{ns} src rows, attention on {qs}/{N} queries (fp32 torch CPU), "
-              f"extrapolated by row fraction")
+    mn, dst, src = match()
+    t_match = time.perf_counter() - t0
+    sub = max(256, src.numel() // 256)
+    t_sim = _t(lambda: (mn[src[:sub]] @ mn[dst].T).max(dim=1)) * src.numel() / sub
+    kv = torch.randn(N, 1024, generator=g)
+    idx = torch.randint(0, dst.numel(), (src.numel(),), generator=g)
+    def merge():
+        for _ in range(2):
+            mid = kv[dst].clone()
+            mid.index_add_(0, idx, kv[src])
+    t_merge = _t(merge)
+    for name, ratio in (("merged_0.98", 0.98), ("merged_0.2", 0.2)):
+        nm_ = merged_len(S, ratio)
+        qq = torch.randn(1, 16, 512, 64, generator=g)
+        kk = torch.randn(1, 16, nm_, 64, generator=g)
+        b = torch.rand(1, 1, 1, nm_, generator=g)
+        t_att = _t(lambda: F.scaled_dot_product_attention(qq, kk, kk, attn_mask=b)) * N / 512
+        parts[f"{name}_per_block"] = t_match + t_sim + t_merge + t_att
+    return parts
+
+
+def cpu_forward_ms(S, vanilla=False):
+    p = cpu_block_parts(S)
+    lin = p["linear_per_block"] * 72                      # 24 DINO + 24 frame + 24 global
+    frame = p["frame_attn_per_block"] * (24 + 24)         # DINO + frame blocks
+    if vanilla:
+        glob = merged_ms = 0.0
+        import torch
+        import torch.nn.functional as F
+        N = S * P_TOK
+        q = torch.randn(1, 16, 512, 64)
+        k = torch.randn(1, 16, N, 64)
+        glob = _t(lambda: F.scaled_dot_product_attention(q, k, k)) * N / 512 * 24
+    else:
+        glob = (9 * (p["frame_attn_per_block"] + p["shared_attn_per_block"])
+                + 11 * p["merged_0.98_per_block"] + 4 * p["merged_0.2_per_block"])
+    total = lin + frame + glob
+    sample = (f"GPA forward at S={S} composed from sampled components on the host cores "
+              f"(torch CPU fp32): linears on 1024 rows, per-frame attention on 1 frame, "
+              f"global/merged attention on 512-2048 query rows, similarity on 1/256 of the src "
+              f"rows, matching and K/V merge at full size; scaled by rows/frames and the block "
+              f"schedule (24 DINO + 24 frame + 9 early + 11 merged + 4 core); heads excluded")
     return total * 1e3, sample
 
 
@@ -223,28 +280,47 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     S = args.frames
-    metric = "GPA merged global block latency (ms) at S=200, 1 B200"
+    fwd = args.workload == "forward"
+    if fwd:
+        workload = f"gpa_vggt_forward_S{S}" + ("_vanilla" if args.vanilla else "")
+        config = {"workload": workload, "model": "VGGT-1B (random init, seed 0)", "frames": S,
+                  "image": "518x518", "tokens_per_global_block": S * P_TOK,
+                  "schedule": "vanilla" if args.vanilla else
+                  "9 frame+shared, 11 merged@0.98, 4 core@0.2 (blocks 9-23)",
+                  "global_batch": 1, "seq_len": S * P_TOK,
+                  "l2": "activations > L2 (no flush needed)"}
+        metric = METRIC
+    else:
+        config = {"workload": f"gpa_merged_block_S{S}", "frames": S, "tokens": S * P_TOK,
+                  "merge_ratio": args.ratio, "heads": 16, "head_dim": 64,
+                  "l2": "inputs > L2 (no flush needed)"}
+        metric = f"GPA merged global block latency (ms) at S={S}"
+    config["parallelism"] = f"replicas x{world}" if world > 1 else "single GPU"
     base = {"metric": metric, "unit": "ms", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "higher_is_better": False, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) tokens)",
-            "config": {"workload": f"gpa_merged_block_S{S}", "frames": S, "tokens": S * P_TOK,
-                       "merge_ratio": args.ratio, "heads": 16, "head_dim": 64, "dim": 1024,
-                       "l2": "inputs > L2 (no flush needed)",
-                       "parallelism": f"replicas x{world}"}}
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (torch.rand frames / seeded N(0,1) tokens, random-init weights)",
+            "config": config}
 
     if args.impl == "reference":
         if rank != 0:
             return
-        ms_list = []
-        sample = ""
-        for _ in range(args.warmup + args.steps):
-            ms, sample = cpu_block_ms(S, args.ratio)
-            ms_list.append(ms)
-        ms = statistics.mean(ms_list[args.warmup:])
+        vals, sample = [], ""
+        for _ in range(max(1, args.warmup) + args.steps):
+            if fwd:
+                ms, sample = cpu_forward_ms(S, args.vanilla)
+            else:
+                p = cpu_block_parts(S)
+                ms = p["merged_0.98_per_block"] * 1e3
+                sample = f"one merged block at S={S}, composed from sampled components"
+            vals.append(ms)
+        ms = statistics.mean(vals[-args.steps:])
         line = dict(base, impl="reference", value=ms, ms_per_step=ms,
                     cpu_baseline={"value": ms, "unit": "ms", "cores": os.cpu_count(), "kind": "port",
                                   "sample": sample},
                     e2e={"value": ms, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
+        if fwd:
+            line["frames_per_s"] = S / (ms / 1e3)
         print(json.dumps(line), flush=True)
         return
 
@@ -252,36 +328,45 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                              device_id=dev)
-    from gpa_vggt_b200 import _lib
+    from gpa_vggt_b200 import _lib, kernels
     _lib.load()
-    x, qkv = make_inputs(S, dev, seed=rank)
-    out = torch.empty(S * P_TOK, 16, 64, device=dev, dtype=torch.bfloat16)
-    for _ in range(args.warmup):
-        _, plan = merged_block(x, qkv, args.ratio, out=out)
-    torch.cuda.synchronize()
-    n_m = plan.n_out
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.steps)]
+    if fwd:
+        model = build_model(dev, args.vanilla)
+        g = torch.Generator(device="cpu").manual_seed(0)
+        images = torch.rand(1, S, 3, 518, 518, generator=g).to(torch.bfloat16).to(dev)
+        step = lambda: forward(model, images)  # noqa: E731
+    else:
+        x, qkv = make_block_inputs(S, dev, seed=rank)
+        out = torch.empty(S * P_TOK, 16, 64, device=dev, dtype=torch.bfloat16)
+        step = lambda: merged_block(x, qkv, args.ratio, out=out)  # noqa: E731
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    kernels.ATTN_TIMING = []
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     l0 = _lib.launch_count()
     with Clocks(local) as clk:
         start.record()
-        for i in range(args.steps):
-            merged_block(x, qkv, args.ratio, out=out, timers=ev[i])
+        for _ in range(args.steps):
+            step()
         stop.record()
         barrier()
     launches = _lib.launch_count() - l0
+    timing, kernels.ATTN_TIMING = kernels.ATTN_TIMING, None
     ms = start.elapsed_time(stop) / args.steps
-    attn_ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+    attn_ms = sum(a.elapsed_time(b) for a, b, _ in timing) / args.steps
+    attn_flops = sum(f for _, _, f in timing) / args.steps
+    n_attn = len(timing) // args.steps
     if world > 1:
         t = torch.tensor([ms, attn_ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -290,29 +375,43 @@ def main():
     # end to end through the public API with host buffers
     e2e = None
     if not args.no_e2e:
-        from gpa_vggt_b200.merging.merge import token_merge_bipartite2d
-        from gpa_vggt_b200.merging.fused_attention import attention_keybias
-        hx = x.cpu().pin_memory()
-        hq = qkv.cpu().pin_memory()
-        hout = torch.empty(S * P_TOK, 1024, dtype=torch.bfloat16).pin_memory()
-        N = S * P_TOK
+        if fwd:
+            h_img = images.cpu().pin_memory()
+            h_pose = torch.empty(1, S, 9, dtype=torch.float32).pin_memory()
+            h_depth = torch.empty(1, S, 518, 518, 1, dtype=torch.float32).pin_memory()
+            h_conf = torch.empty(1, S, 518, 518, dtype=torch.float32).pin_memory()
 
-        def e2e_step():
-            dx = hx.to(dev, non_blocking=True)
-            dq = hq.to(dev, non_blocking=True)
-            gen = torch.Generator(device=dev)
-            gen.manual_seed(33)
-            m = token_merge_bipartite2d(dx[None], 37, 37, 2, 2, int(N * args.ratio), False, gen,
-                                        metric_dim=128, num_special=5)
-            qq = dq[:, 0].transpose(0, 1)[None]
-            kk = m.heads(dq[:, 1].transpose(0, 1)[None])
-            vv = m.heads(dq[:, 2].transpose(0, 1)[None])
-            bias = m.size.log().reshape(1, 1, 1, -1)
-            o = attention_keybias(qq, kk, vv, bias, 64 ** -0.5)
-            hout.copy_(o[0].transpose(0, 1).reshape(N, 1024), non_blocking=True)
+            def e2e_step():
+                d_img = h_img.to(dev, non_blocking=True)
+                pose, depth, conf = forward(model, d_img)
+                h_pose.copy_(pose, non_blocking=True)
+                h_depth.copy_(depth, non_blocking=True)
+                h_conf.copy_(conf, non_blocking=True)
 
-        for _ in range(2):
-            e2e_step()
+            h2d = h_img.numel() * h_img.element_size()
+            d2h = sum(t.numel() * t.element_size() for t in (h_pose, h_depth, h_conf))
+        else:
+            from gpa_vggt_b200.merging.merge import token_merge_bipartite2d
+            from gpa_vggt_b200.merging.fused_attention import attention_keybias
+            hx, hq = x.cpu().pin_memory(), qkv.cpu().pin_memory()
+            N = S * P_TOK
+            hout = torch.empty(N, 1024, dtype=torch.bfloat16).pin_memory()
+
+            def e2e_step():
+                dx, dq = hx.to(dev, non_blocking=True), hq.to(dev, non_blocking=True)
+                gen = torch.Generator(device=dev)
+                gen.manual_seed(33)
+                m = token_merge_bipartite2d(dx[None], 37, 37, 2, 2, int(N * args.ratio), False, gen,
+                                            metric_dim=128, num_special=5)
+                o = attention_keybias(dq[:, 0].transpose(0, 1)[None],
+                                      m.heads(dq[:, 1].transpose(0, 1)[None]),
+                                      m.heads(dq[:, 2].transpose(0, 1)[None]),
+                                      m.size.log().reshape(1, 1, 1, -1), 64 ** -0.5)
+                hout.copy_(o[0].transpose(0, 1).reshape(N, 1024), non_blocking=True)
+
+            h2d = (hx.numel() + hq.numel()) * 2
+            d2h = hout.numel() * 2
+        e2e_step()
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -325,22 +424,28 @@ def main():
             t = torch.tensor([e_ms], device=dev)
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             e_ms = t.item()
-        e2e = {"value": e_ms, "unit": "ms", "h2d_bytes_per_step": hx.numel() * 2 + hq.numel() * 2,
-               "d2h_bytes_per_step": hout.numel() * 2}
+        e2e = {"value": e_ms, "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+        if fwd:
+            e2e["frames_per_s"] = world * S / (e_ms / 1e3)
 
     pk = peaks()
-    fl = attn_flops(S, n_m)
-    achieved = fl / (attn_ms * 1e-3) / 1e12
-    roof = {"kernel": "gpa_attention_keybias (attn_kernel)", "bound": "tensor",
-            "achieved": achieved, "peak": pk["bf16_sus"], "unit": "TFLOP/s",
-            "frac": achieved / pk["bf16_sus"], "peak_kind": f"{pk['src']} sustained bf16",
-            "frac_of_burst": achieved / pk["bf16"],
-            "flops_per_launch": fl, "ms_per_launch": attn_ms, "traffic": None}
-    line = dict(base, value=ms, ms_per_step=ms, n_m=n_m, gpu_launches=launches,
-                roofline=roof, e2e=e2e, clocks=clk.summary())
-    line["config"]["n_m"] = n_m
+    achieved = attn_flops / (attn_ms * 1e-3) / 1e12
+    roof = {"kernel": "attn_kernel (gpa_attention_keybias), all launches of a step",
+            "bound": "tensor", "achieved": achieved, "peak": pk["bf16_sus"], "unit": "TFLOP/s",
+            "frac": achieved / pk["bf16_sus"], "peak_kind": f"{pk['src']} sustained bf16 (long step)",
+            "frac_of_burst": achieved / pk["bf16"], "flops_per_step": attn_flops,
+            "launches_per_step": n_attn, "ms_per_step": attn_ms,
+            "share_of_step": attn_ms / ms, "traffic": None}
+    line = dict(base, value=ms, ms_per_step=ms, gpu_launches=launches, roofline=roof, e2e=e2e,
+                clocks=clk.summary())
+    if fwd:
+        line["frames_per_s"] = world * S / (ms / 1e3)
+        line["gpu_memory_peak_gib"] = torch.cuda.max_memory_allocated(dev) / 2 ** 30
     if rank == 0 and not args.no_cpu:
-        cms, sample = cpu_block_ms(S, args.ratio)
+        if fwd:
+            cms, sample = cpu_forward_ms(S, args.vanilla)
+        else:
+            cms, sample = cpu_block_parts(S)["merged_0.98_per_block"] * 1e3, f"merged block at S={S}"
         line["cpu_baseline"] = {"value": cms, "unit": "ms", "cores": os.cpu_count(), "kind": "port",
                                 "sample": sample}
     if world > 1:

@@ -24,6 +24,11 @@ F32 = torch.float32
 CHECK_STATUS = os.environ.get("GPA_CHECK_STATUS", "0") == "1"
 
 
+# When set to a list, every attention launch appends (start event, end event,
+# algorithmic flops) recorded on its stream (used by bench.py for the roofline).
+ATTN_TIMING = None
+
+
 class KernelTimeout(RuntimeError):
     """A kernel's pipeline wait gave up (device status word set)."""
 
@@ -203,12 +208,19 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bias: Optional[
         out = torch.empty(B, H, M, D, device=q.device, dtype=BF16)
     lse = torch.empty(B, H, M, device=q.device, dtype=F32) if return_lse else None
     status, own = _status_word(status, q.device)
+    timing = ATTN_TIMING
+    if timing is not None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
     call("gpa_attention_keybias", ptr(q), ptr(k), ptr(v), ptr(bias), B, H, M, N, D,
          q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
          v.stride(0), v.stride(1), v.stride(2), bsb, bsh, float(sm_scale), ptr(out),
          out.stride(0), out.stride(1), out.stride(2), ptr(lse),
          lse.stride(0) if lse is not None else 0, lse.stride(1) if lse is not None else 0,
          ptr(status), stream_of(q))
+    if timing is not None:
+        e1.record()
+        timing.append((e0, e1, 4.0 * B * H * M * N * D))
     if own:
         _check_status(status, "gpa_attention_keybias")
     return (out, lse) if return_lse else out

@@ -1,0 +1,284 @@
+"""Transformer layers of VGGT around the GPA attention path.
+
+Module and parameter names follow the reference (vggt/layers/*.py) so that one
+state_dict loads into either model.  Every head_dim-64 attention runs on the
+sm_100a kernels: the GPA global paths (merged, frame + shared set), the plain
+global/frame attention and the DINO blocks.  Everything else (linears, norms,
+activations) is ordinary torch, run under bf16 autocast as the reference's
+evaluation does (eval/bench_e2e.py:90-95).
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .. import kernels
+from ..merging.merge import build_plan
+
+BF16 = torch.bfloat16
+
+
+# ---------------------------------------------------------------------------
+# small layers (vggt/layers/mlp.py, layer_scale.py, patch_embed.py)
+# ---------------------------------------------------------------------------
+class Mlp(nn.Module):
+    def __init__(self, in_features, hidden_features=None, out_features=None, act_layer=nn.GELU,
+                 drop=0.0, bias=True):
+        super().__init__()
+        out_features = out_features or in_features
+        hidden_features = hidden_features or in_features
+        self.fc1 = nn.Linear(in_features, hidden_features, bias=bias)
+        self.act = act_layer()
+        self.fc2 = nn.Linear(hidden_features, out_features, bias=bias)
+
+    def forward(self, x):
+        return self.fc2(self.act(self.fc1(x)))
+
+
+class LayerScale(nn.Module):
+    def __init__(self, dim, init_values=1e-5):
+        super().__init__()
+        self.gamma = nn.Parameter(init_values * torch.ones(dim))
+
+    def forward(self, x):
+        return x * self.gamma
+
+
+class PatchEmbed(nn.Module):
+    """Conv patchifier: [B, 3, H, W] -> [B, H/p * W/p, C]."""
+
+    def __init__(self, img_size=224, patch_size=16, in_chans=3, embed_dim=768):
+        super().__init__()
+        self.patch_size = (patch_size, patch_size)
+        self.num_patches = (img_size // patch_size) ** 2
+        self.proj = nn.Conv2d(in_chans, embed_dim, kernel_size=patch_size, stride=patch_size)
+        self.norm = nn.Identity()
+
+    def forward(self, x):
+        return self.proj(x).flatten(2).transpose(1, 2)
+
+
+# ---------------------------------------------------------------------------
+# 2D rotary embedding (vggt/layers/rope.py), token-major layout
+# ---------------------------------------------------------------------------
+class PositionGetter:
+    """(y, x) patch coordinates of an h x w grid, [batch, h*w, 2] (rope.py:24-65)."""
+
+    def __init__(self):
+        self.cache = {}
+
+    def __call__(self, batch_size, height, width, device):
+        key = (height, width, str(device))
+        if key not in self.cache:
+            ys = torch.arange(height, device=device)
+            xs = torch.arange(width, device=device)
+            self.cache[key] = torch.cartesian_prod(ys, xs)
+        return self.cache[key].view(1, height * width, 2).expand(batch_size, -1, -1).clone()
+
+
+class RotaryPositionEmbedding2D(nn.Module):
+    """First half of each head's features rotates with y, second half with x;
+    within a half, the rotate-half convention with base frequency 100
+    (rope.py:68-209).  Operates on [B, N, H, D] tokens with [B, N, 2] positions."""
+
+    def __init__(self, frequency: float = 100.0, scaling_factor: float = 1.0):
+        super().__init__()
+        self.base_frequency = frequency
+        self.scaling_factor = scaling_factor
+        self.cache = {}
+
+    def _tables(self, dim, n_pos, device, dtype):
+        key = (dim, n_pos, str(device), dtype)
+        if key not in self.cache:
+            inv = 1.0 / (self.base_frequency ** (torch.arange(0, dim, 2, device=device) / dim))
+            ang = torch.outer(torch.arange(n_pos, device=device, dtype=inv.dtype), inv).to(dtype)
+            ang = torch.cat((ang, ang), dim=-1)
+            self.cache[key] = (ang.cos().to(dtype), ang.sin().to(dtype))
+        return self.cache[key]
+
+    @staticmethod
+    def _rot(t):
+        h = t.shape[-1] // 2
+        return torch.cat((-t[..., h:], t[..., :h]), dim=-1)
+
+    def forward(self, tokens: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
+        half = tokens.shape[-1] // 2
+        n_pos = int(positions.max()) + 1
+        cos, sin = self._tables(half, n_pos, tokens.device, tokens.dtype)
+        pos = positions.long()
+        out = []
+        for i, t in enumerate(tokens.chunk(2, dim=-1)):
+            c = F.embedding(pos[..., i], cos)[:, :, None, :]   # [B, N, 1, half]
+            s = F.embedding(pos[..., i], sin)[:, :, None, :]
+            out.append(t * c + self._rot(t) * s)
+        return torch.cat(out, dim=-1)
+
+
+# ---------------------------------------------------------------------------
+# attention (vggt/layers/attention.py)
+# ---------------------------------------------------------------------------
+class Attention(nn.Module):
+    """VGGT attention with the two GPA global paths on the sm_100a kernels.
+
+    Attributes set by the aggregator, as in the reference (attention.py:53-63):
+    ``frame_special``, ``num_special``, ``broadcast_pool``, ``merge_grid``,
+    ``merge_metric_dim``, ``merge_ratio``, ``patch_width``, ``patch_height``.
+    Tests may set ``rng_override = (rand_idx, proj)`` to inject the two random
+    draws of the merge (a CPU run draws different numbers than a CUDA run).
+    """
+
+    def __init__(self, dim, num_heads=8, qkv_bias=True, proj_bias=True, attn_drop=0.0,
+                 proj_drop=0.0, norm_layer=nn.LayerNorm, qk_norm=False, fused_attn=True, rope=None,
+                 patch_width=37, patch_height=28, merge_ratio=0.9):
+        super().__init__()
+        assert dim % num_heads == 0
+        self.num_heads = num_heads
+        self.head_dim = dim // num_heads
+        self.scale = self.head_dim ** -0.5
+        self.patch_width = patch_width
+        self.patch_height = patch_height
+        self.merge_ratio = merge_ratio
+        self.frame_special = False
+        self.num_special = 5
+        self.broadcast_pool = 0
+        self.merge_grid = 2
+        self.merge_metric_dim = 0
+        self.rng_override = None
+        self.qkv = nn.Linear(dim, dim * 3, bias=qkv_bias)
+        self.q_norm = norm_layer(self.head_dim) if qk_norm else nn.Identity()
+        self.k_norm = norm_layer(self.head_dim) if qk_norm else nn.Identity()
+        self.proj = nn.Linear(dim, dim, bias=proj_bias)
+        self.rope = rope
+
+    # -- helpers ------------------------------------------------------------
+    def _qkv(self, x, pos):
+        B, N, C = x.shape
+        qkv = self.qkv(x).reshape(B, N, 3, self.num_heads, self.head_dim)
+        q, k, v = qkv.unbind(2)                      # [B, N, H, D] views
+        q, k = self.q_norm(q), self.k_norm(k)
+        if self.rope is not None:
+            q, k = self.rope(q, pos), self.rope(k, pos)
+        return q, k, v
+
+    @staticmethod
+    def _heads(t):
+        """[B, N, H, D] -> [B, H, N, D] view (no copy)."""
+        return t.permute(0, 2, 1, 3)
+
+    def forward(self, x: torch.Tensor, pos=None, global_merging=None) -> torch.Tensor:
+        B, N, C = x.shape
+        q, k, v = self._qkv(x, pos)
+        if self.frame_special:
+            out = frame_special_attention(q.to(BF16), k.to(BF16), v.to(BF16), self)
+        elif global_merging is not None:
+            out = merged_attention(x, q, k, v, self)
+        else:
+            out = torch.empty(B, N, self.num_heads, self.head_dim, device=x.device, dtype=BF16)
+            kernels.attention(self._heads(q.to(BF16)), self._heads(k.to(BF16)),
+                              self._heads(v.to(BF16)), None, self.scale, out=self._heads(out))
+        return self.proj(out.reshape(B, N, C))
+
+
+def merged_attention(x, q, k, v, attn: Attention) -> torch.Tensor:
+    """Query-preserving K/V merging (attention.py:233-268): merge K/V into the
+    dst tokens matched on the 128-d projected x, then attend with +log(count)."""
+    B, N, C = x.shape
+    H, D = attn.num_heads, attn.head_dim
+    if B != 1:
+        raise NotImplementedError("merged_attention: batch size 1 (the reference's eval setting)")
+    r = int(N * attn.merge_ratio)
+    rand_idx = proj = None
+    gen = None
+    if attn.rng_override is not None:
+        rand_idx, proj = attn.rng_override
+    else:
+        gen = torch.Generator(device=x.device)
+        gen.manual_seed(33)
+    plan = build_plan(x[0], attn.patch_width, attn.patch_height, attn.merge_grid, attn.merge_grid, r,
+                      False, gen, attn.merge_metric_dim, attn.num_special, rand_idx=rand_idx,
+                      proj=proj)
+    # K keeps its dtype through the merge (fp32 after qk-LayerNorm under autocast),
+    # then both are bf16 for the attention, as attention_keybias casts them.
+    km = kernels.merge_kv(k[0].transpose(0, 1), plan)          # [H, N_m, D]
+    vm = kernels.merge_kv(v[0].transpose(0, 1), plan)
+    bias = plan.counts.log().to(BF16).float()                  # rounded like the reference
+    out = torch.empty(1, N, H, D, device=x.device, dtype=BF16)
+    kernels.attention(q.to(BF16).permute(0, 2, 1, 3), km.to(BF16)[None], vm.to(BF16)[None],
+                      bias[None, None], attn.scale, out=out.permute(0, 2, 1, 3))
+    return out
+
+
+def frame_special_attention(q, k, v, attn: Attention) -> torch.Tensor:
+    """Frame attention plus the shared cross-frame K/V set (attention.py:73-206):
+    own-frame keys (with log2 row sums), then every frame's special tokens and
+    pooled patch summaries (bias +log size), combined exactly by log-sum-exp.
+    q, k, v: [1, N, H, D] bf16 -> [1, N, H, D] bf16."""
+    B, N, H, D = q.shape
+    if B != 1:
+        raise NotImplementedError("frame_special_attention: batch size 1")
+    pts, pw, ph, kp = attn.num_special, attn.patch_width, attn.patch_height, attn.broadcast_pool
+    P = pw * ph + pts
+    S = N // P
+    if S * P != N:
+        raise ValueError(f"frame_special: token count {N} is not S*(patch_w*patch_h+{pts})")
+    if kp <= 0:
+        raise NotImplementedError("frame_special_attention: broadcast_pool > 0 only")
+    q5, k5, v5 = (t.view(S, P, H, D) for t in (q[0], k[0], v[0]))
+    # (a) own-frame patch keys, batch = frames
+    out_a = torch.empty(S, P, H, D, device=q.device, dtype=BF16)
+    _, lse_a = kernels.attention(q5.permute(0, 2, 1, 3), k5[:, pts:].permute(0, 2, 1, 3),
+                                 v5[:, pts:].permute(0, 2, 1, 3), None, attn.scale,
+                                 return_lse=True, out=out_a.permute(0, 2, 1, 3))
+    # (b) shared set: specials of every frame, then the pooled summaries
+    kh, vh = k[0].transpose(0, 1), v[0].transpose(0, 1)       # [H, N, D] views
+    pk, pv, size = kernels.frame_pool(kh, vh, S, ph, pw, pts, kp)
+    sk = torch.cat([k5[:, :pts].permute(2, 0, 1, 3).reshape(H, S * pts, D), pk], 1)
+    sv = torch.cat([v5[:, :pts].permute(2, 0, 1, 3).reshape(H, S * pts, D), pv], 1)
+    bias = torch.cat([torch.zeros(H, S * pts, device=q.device), size.log()], 1)
+    bias = bias.to(BF16).float()                               # the reference casts it to bf16
+    out_b, lse_b = kernels.attention(q[0].transpose(0, 1)[None], sk[None], sv[None], bias[None],
+                                     attn.scale, return_lse=True)
+    # (c) exact combine into token-major [N, H, D]
+    out = torch.empty(S, P, H, D, device=q.device, dtype=BF16)
+    kernels.lse_combine(out_a.permute(2, 0, 1, 3), lse_a.permute(1, 0, 2),
+                        out_b[0].view(H, S, P, D), lse_b[0].view(H, S, P),
+                        out=out.permute(2, 0, 1, 3))
+    return out.view(1, N, H, D)
+
+
+class SdpaAttention(Attention):
+    """Plain attention through torch SDPA, for the camera head's trunk
+    (head_dim 128, S tokens; outside the GPA path)."""
+
+    def forward(self, x, pos=None, global_merging=None):
+        B, N, C = x.shape
+        q, k, v = self._qkv(x, pos)
+        o = F.scaled_dot_product_attention(self._heads(q), self._heads(k), self._heads(v))
+        return self.proj(o.transpose(1, 2).reshape(B, N, C))
+
+
+# ---------------------------------------------------------------------------
+# block (vggt/layers/block.py:23-96)
+# ---------------------------------------------------------------------------
+class Block(nn.Module):
+    def __init__(self, dim, num_heads, mlp_ratio=4.0, qkv_bias=True, proj_bias=True, ffn_bias=True,
+                 drop=0.0, attn_drop=0.0, init_values=None, drop_path=0.0, act_layer=nn.GELU,
+                 norm_layer=nn.LayerNorm, attn_class=Attention, ffn_layer=Mlp, qk_norm=False,
+                 fused_attn=True, rope=None, merge_ratio=0.9):
+        super().__init__()
+        self.norm1 = norm_layer(dim)
+        self.attn = attn_class(dim, num_heads=num_heads, qkv_bias=qkv_bias, proj_bias=proj_bias,
+                               qk_norm=qk_norm, rope=rope, merge_ratio=merge_ratio)
+        self.ls1 = LayerScale(dim, init_values=init_values) if init_values else nn.Identity()
+        self.norm2 = norm_layer(dim)
+        self.mlp = ffn_layer(in_features=dim, hidden_features=int(dim * mlp_ratio),
+                             act_layer=act_layer, bias=ffn_bias)
+        self.ls2 = LayerScale(dim, init_values=init_values) if init_values else nn.Identity()
+
+    def forward(self, x, pos=None, global_merging=None):
+        x = x + self.ls1(self.attn(self.norm1(x), pos=pos, global_merging=global_merging))
+        return x + self.ls2(self.mlp(self.norm2(x)))

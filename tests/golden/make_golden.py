@@ -253,7 +253,76 @@ def gen_block():
                     out_merged=out_merged[0], out_plain=out_plain[0]), OUT / "block_small.pt")
 
 
+def gen_model_bf16(S=2):
+    """The reference's own bf16 drift: the same forward as gen_model, with the
+    model in bf16 under CPU bf16 autocast, stored beside the fp32 result."""
+    sys.path.insert(0, str(OUT.parents[1]))
+    from gpa_vggt_b200.vggt.model import init_weights
+    from vggt.models.vggt import VGGT as RefVGGT
+    model = RefVGGT()
+    init_weights(model, seed=0)
+    model = model.eval().to(torch.bfloat16)
+    model.update_patch_dimensions(37, 37)
+    images = torch.rand(1, S, 3, 518, 518, generator=torch.Generator().manual_seed(0))
+    stock = ref_merge.fast_similarity_chunks
+
+    def matcher(a, bT, chunk):
+        nm, ni = interp_sim_argmax(a.float(), bT.transpose(-1, -2).float())
+        return nm.to(a.dtype), ni
+
+    ref_merge.fast_similarity_chunks = matcher
+    try:
+        with torch.no_grad(), torch.autocast("cpu", dtype=torch.bfloat16):
+            out = model(images.to(torch.bfloat16))
+    finally:
+        ref_merge.fast_similarity_chunks = stock
+    torch.save(dict(S=S, pose_enc=out["pose_enc"].float().clone(),
+                    depth=out["depth"].half().clone(), depth_conf=out["depth_conf"].half().clone()),
+               OUT / f"model_s{S}_bf16.pt")
+
+
+def gen_model(S=2):
+    """Full VGGT (GPA configuration) forward on CPU, fp32, with the weights of
+    gpa_vggt_b200.vggt.init_weights(seed=0) (a function of parameter names and
+    shapes only, so the GPU test rebuilds the same weights)."""
+    sys.path.insert(0, str(OUT.parents[1]))
+    from gpa_vggt_b200.vggt.model import init_weights
+    from vggt.models.vggt import VGGT as RefVGGT
+    torch.manual_seed(0)
+    model = RefVGGT()
+    init_weights(model, seed=0)
+    model.eval()
+    model.update_patch_dimensions(37, 37)
+    images = torch.rand(1, S, 3, 518, 518, generator=torch.Generator().manual_seed(0))
+    stock = ref_merge.fast_similarity_chunks
+
+    def matcher(a, bT, chunk):
+        nm, ni = interp_sim_argmax(a, bT.transpose(-1, -2))
+        return nm.to(a.dtype), ni
+
+    ref_merge.fast_similarity_chunks = matcher
+    try:
+        with torch.no_grad():
+            out = model(images)
+    finally:
+        ref_merge.fast_similarity_chunks = stock
+    g = torch.Generator().manual_seed(33)
+    rand_idx = torch.randint(4, size=(S - 1, 18, 18), generator=g)
+    gp = torch.Generator().manual_seed(ref_merge.PROJ_SEED)
+    proj = torch.randn(1024, 128, dtype=torch.float32, generator=gp)
+    torch.save(dict(S=S, image_seed=0, weight_seed=0, rand_idx=rand_idx, proj=proj,
+                    pose_enc=out["pose_enc"].clone(),
+                    depth=out["depth"].half().clone(), depth_conf=out["depth_conf"].half().clone()),
+               OUT / f"model_s{S}.pt")
+
+
 if __name__ == "__main__":
+    if len(sys.argv) > 1 and sys.argv[1] == "model":
+        gen_model()
+        sys.exit(0)
+    if len(sys.argv) > 1 and sys.argv[1] == "model_bf16":
+        gen_model_bf16()
+        sys.exit(0)
     gen_merge()
     gen_attention()
     gen_frame()
