@@ -1,0 +1,233 @@
+// Normalisation work of the attention blocks, fused and HBM-bound:
+//  * gpa_layernorm_bf16: LayerNorm of bf16 rows with fp32 statistics and a
+//    bf16 result (the value a bf16-autocast Linear receives after the
+//    reference's fp32 LayerNorm, vggt/layers/block.py:85-92).
+//  * gpa_qk_norm_rope: per-head LayerNorm of q and k (qk_norm) followed by the
+//    2D rotary embedding (vggt/layers/attention.py:216-220, rope.py:139-209),
+//    in fp32 registers, written back as bf16 -- one pass over the qkv buffer
+//    instead of the norm, rotate, concatenate and cast kernels.
+#include "common.cuh"
+#include "capi_util.h"
+
+namespace gpa {
+namespace norm {
+
+template <typename W>
+__device__ __forceinline__ float ldw(const W* p, int i);
+template <>
+__device__ __forceinline__ float ldw<float>(const float* p, int i) { return p[i]; }
+template <>
+__device__ __forceinline__ float ldw<__nv_bfloat16>(const __nv_bfloat16* p, int i) {
+  return __bfloat162float(p[i]);
+}
+
+// One warp per row; cols % 256 == 0, cols <= 4096 (16-byte vectors per lane).
+template <int VPL, typename W>
+__global__ void __launch_bounds__(256) layernorm_kernel(const __nv_bfloat16* __restrict__ x,
+                                                        int64_t xs, int rows, const W* __restrict__ w,
+                                                        const W* __restrict__ b, float eps,
+                                                        __nv_bfloat16* __restrict__ out, int64_t os) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  constexpr int C = VPL * 256;
+  const __nv_bfloat16* xr = x + (int64_t)row * xs;
+  float v[VPL][8];
+  float s = 0.f;
+#pragma unroll
+  for (int u = 0; u < VPL; ++u) {
+    uint4 raw = __ldg(reinterpret_cast<const uint4*>(xr) + u * 32 + lane);
+    const __nv_bfloat162* e = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 f = __bfloat1622float2(e[i]);
+      v[u][2 * i] = f.x;
+      v[u][2 * i + 1] = f.y;
+      s += f.x + f.y;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / C;
+  float q = 0.f;
+#pragma unroll
+  for (int u = 0; u < VPL; ++u)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float d = v[u][i] - mean;
+      q = fmaf(d, d, q);
+    }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float rstd = rsqrtf(q / C + eps);
+  __nv_bfloat16* orow = out + (int64_t)row * os;
+#pragma unroll
+  for (int u = 0; u < VPL; ++u) {
+    const int c0 = (u * 32 + lane) * 8;
+    uint4 raw;
+    __nv_bfloat162* e = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float y0 = fmaf((v[u][2 * i] - mean) * rstd, ldw(w, c0 + 2 * i), ldw(b, c0 + 2 * i));
+      const float y1 = fmaf((v[u][2 * i + 1] - mean) * rstd, ldw(w, c0 + 2 * i + 1), ldw(b, c0 + 2 * i + 1));
+      e[i] = __floats2bfloat162_rn(y0, y1);
+    }
+    reinterpret_cast<uint4*>(orow)[u * 32 + lane] = raw;
+  }
+}
+
+// One thread per 64-wide head row of q or k.  Rotary layout: dims 0..31 turn
+// with the row coordinate, 32..63 with the column coordinate; inside each half
+// the rotate-half pairing (i, i+16).  cos/sin tables: [n_pos, 32] fp32.
+template <typename W>
+__global__ void __launch_bounds__(256) qk_norm_rope_kernel(
+    const __nv_bfloat16* __restrict__ qkv, int64_t tok_stride, int64_t q_off, int64_t k_off,
+    int tokens, int heads, const W* __restrict__ qw, const W* __restrict__ qb,
+    const W* __restrict__ kw, const W* __restrict__ kb, float eps, const int64_t* __restrict__ pos,
+    const float* __restrict__ cos_tab, const float* __restrict__ sin_tab, int n_pos,
+    __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_out, int64_t out_tok_stride) {
+  __shared__ float s_w[2][64], s_b[2][64];
+  if (threadIdx.x < 64) {
+    s_w[0][threadIdx.x] = qw ? ldw(qw, threadIdx.x) : 1.f;
+    s_b[0][threadIdx.x] = qb ? ldw(qb, threadIdx.x) : 0.f;
+    s_w[1][threadIdx.x] = kw ? ldw(kw, threadIdx.x) : 1.f;
+    s_b[1][threadIdx.x] = kb ? ldw(kb, threadIdx.x) : 0.f;
+  }
+  __syncthreads();
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t per = (int64_t)tokens * heads;
+  if (gid >= 2 * per) return;
+  const int which = gid >= per;  // 0 = q, 1 = k
+  const int64_t r = gid - which * per;
+  const int64_t tok = r / heads;
+  const int hh = (int)(r - tok * heads);
+  const __nv_bfloat16* src = qkv + tok * tok_stride + (which ? k_off : q_off) + hh * 64;
+  float v[64];
+  float s = 0.f;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    uint4 raw = reinterpret_cast<const uint4*>(src)[u];  // may be rewritten in place: no nc path
+    const __nv_bfloat162* e = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 f = __bfloat1622float2(e[i]);
+      v[8 * u + 2 * i] = f.x;
+      v[8 * u + 2 * i + 1] = f.y;
+      s += f.x + f.y;
+    }
+  }
+  const float mean = s * (1.f / 64.f);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < 64; ++i) {
+    const float d = v[i] - mean;
+    q = fmaf(d, d, q);
+  }
+  const float rstd = rsqrtf(q * (1.f / 64.f) + eps);
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = fmaf((v[i] - mean) * rstd, s_w[which][i], s_b[which][i]);
+  if (pos) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      int p = (int)pos[tok * 2 + half];
+      p = min(max(p, 0), n_pos - 1);
+      const float* c = cos_tab + (int64_t)p * 32;
+      const float* sn = sin_tab + (int64_t)p * 32;
+      float* t = v + half * 32;
+      float o[32];
+      // separate roundings of the two products and the sum, as t*cos + rot(t)*sin
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        o[i] = __fadd_rn(__fmul_rn(t[i], c[i]), __fmul_rn(-t[i + 16], sn[i]));
+        o[i + 16] = __fadd_rn(__fmul_rn(t[i + 16], c[i + 16]), __fmul_rn(t[i], sn[i + 16]));
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) t[i] = o[i];
+    }
+  }
+  __nv_bfloat16* dst = (which ? k_out : q_out) + tok * out_tok_stride + hh * 64;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    uint4 raw;
+    __nv_bfloat162* e = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) e[i] = __floats2bfloat162_rn(v[8 * u + 2 * i], v[8 * u + 2 * i + 1]);
+    reinterpret_cast<uint4*>(dst)[u] = raw;
+  }
+}
+
+}  // namespace norm
+}  // namespace gpa
+
+using namespace gpa;
+
+extern "C" int gpa_layernorm_bf16(const void* x, int64_t x_stride, int rows, int cols,
+                                  const void* weight, const void* bias, int param_dtype, float eps,
+                                  void* out, int64_t out_stride, void* stream) {
+  if (rows < 0 || cols <= 0 || cols % 256 || cols > 4096)
+    return fail(GPA_ERR_UNSUPPORTED, "gpa_layernorm_bf16: cols must be a multiple of 256, <= 4096");
+  if (x_stride % 8 || out_stride % 8 || !aligned16(x) || !aligned16(out) || !weight || !bias)
+    return fail(GPA_ERR_INVALID, "gpa_layernorm_bf16: 16-byte aligned rows and weight/bias required");
+  if (param_dtype != GPA_DTYPE_F32 && param_dtype != GPA_DTYPE_BF16)
+    return fail(GPA_ERR_INVALID, "gpa_layernorm_bf16: weight dtype must be f32 or bf16");
+  if (rows == 0) return ok();
+  dim3 grid((rows + 7) / 8);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int vpl = cols / 256;
+#define GPA_LN(V, W)                                                                        \
+  norm::layernorm_kernel<V, W><<<grid, 256, 0, st>>>((const __nv_bfloat16*)x, x_stride, rows, \
+                                                     (const W*)weight, (const W*)bias, eps,    \
+                                                     (__nv_bfloat16*)out, out_stride)
+#define GPA_LN_V(W)                                                            \
+  switch (vpl) {                                                               \
+    case 1: GPA_LN(1, W); break;                                               \
+    case 2: GPA_LN(2, W); break;                                               \
+    case 4: GPA_LN(4, W); break;                                               \
+    case 8: GPA_LN(8, W); break;                                               \
+    case 16: GPA_LN(16, W); break;                                             \
+    default: return fail(GPA_ERR_UNSUPPORTED, "gpa_layernorm_bf16: cols %d", cols); \
+  }
+  if (param_dtype == GPA_DTYPE_BF16) {
+    GPA_LN_V(__nv_bfloat16)
+  } else {
+    GPA_LN_V(float)
+  }
+#undef GPA_LN_V
+#undef GPA_LN
+  return check_launch("gpa_layernorm_bf16");
+}
+
+extern "C" int gpa_qk_norm_rope(const void* qkv, int64_t token_stride, int64_t q_offset,
+                                int64_t k_offset, int tokens, int heads, int head_dim,
+                                const void* q_weight, const void* q_bias, const void* k_weight,
+                                const void* k_bias, int param_dtype, float eps,
+                                const int64_t* positions, const float* cos_table,
+                                const float* sin_table, int n_pos, void* q_out, void* k_out,
+                                int64_t out_token_stride, void* stream) {
+  if (head_dim != 64) return fail(GPA_ERR_UNSUPPORTED, "gpa_qk_norm_rope: head_dim must be 64");
+  if (tokens < 0 || heads <= 0) return fail(GPA_ERR_INVALID, "gpa_qk_norm_rope: bad sizes");
+  if (token_stride % 8 || q_offset % 8 || k_offset % 8 || out_token_stride % 8 || !aligned16(qkv) ||
+      !aligned16(q_out) || !aligned16(k_out))
+    return fail(GPA_ERR_INVALID, "gpa_qk_norm_rope: 16-byte aligned rows required");
+  if (positions && (!cos_table || !sin_table || n_pos <= 0))
+    return fail(GPA_ERR_INVALID, "gpa_qk_norm_rope: rotary tables missing");
+  if (param_dtype != GPA_DTYPE_F32 && param_dtype != GPA_DTYPE_BF16)
+    return fail(GPA_ERR_INVALID, "gpa_qk_norm_rope: weight dtype must be f32 or bf16");
+  const int64_t rows = 2ll * tokens * heads;
+  if (rows == 0) return ok();
+  const unsigned blocks = (unsigned)((rows + 255) / 256);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (param_dtype == GPA_DTYPE_BF16)
+    norm::qk_norm_rope_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+        (const __nv_bfloat16*)qkv, token_stride, q_offset, k_offset, tokens, heads,
+        (const __nv_bfloat16*)q_weight, (const __nv_bfloat16*)q_bias, (const __nv_bfloat16*)k_weight,
+        (const __nv_bfloat16*)k_bias, eps, positions, cos_table, sin_table, n_pos,
+        (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_out, out_token_stride);
+  else
+    norm::qk_norm_rope_kernel<float><<<blocks, 256, 0, st>>>(
+        (const __nv_bfloat16*)qkv, token_stride, q_offset, k_offset, tokens, heads,
+        (const float*)q_weight, (const float*)q_bias, (const float*)k_weight, (const float*)k_bias,
+        eps, positions, cos_table, sin_table, n_pos, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_out,
+        out_token_stride);
+  return check_launch("gpa_qk_norm_rope");
+}

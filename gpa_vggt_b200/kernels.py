@@ -257,3 +257,41 @@ def lse_combine(oa, la, ob, lb, out=None):
          ptr(ob), A(ob.stride()[:3]), ptr(lb), A(lb.stride()), ptr(out), A(out.stride()[:3]),
          stream_of(oa))
     return out
+
+
+def layernorm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """bf16 LayerNorm over the last dim (fp32 statistics) -> bf16."""
+    require_cuda(x, weight, bias, what="layernorm")
+    C = x.shape[-1]
+    x2 = x.reshape(-1, C)
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 or not aligned(x2):
+        x2 = x2.contiguous()
+    if out is None:
+        out = torch.empty(x.shape, device=x.device, dtype=BF16)
+    o2 = out.view(-1, C)
+    call("gpa_layernorm_bf16", ptr(x2), x2.stride(0), x2.shape[0], C, ptr(weight), ptr(bias),
+         _dt(weight), float(eps), ptr(o2), o2.stride(0), stream_of(x))
+    return out
+
+
+def qk_norm_rope(qkv: torch.Tensor, q_norm, k_norm, positions: Optional[torch.Tensor],
+                 cos_table: Optional[torch.Tensor], sin_table: Optional[torch.Tensor]):
+    """In place on qkv [T, 3, H, 64] (bf16, contiguous): q, k <- rope(LN(q)), rope(LN(k)).
+    Returns the (q, k, v) views [T, H, 64]."""
+    require_cuda(qkv, what="qk_norm_rope")
+    T, three, H, D = qkv.shape
+    if three != 3 or not qkv.is_contiguous() or qkv.dtype != BF16:
+        raise ValueError("qk_norm_rope: qkv must be a contiguous bf16 [T, 3, H, D] tensor")
+    qw = getattr(q_norm, "weight", None)
+    qb = getattr(q_norm, "bias", None)
+    kw = getattr(k_norm, "weight", None)
+    kb = getattr(k_norm, "bias", None)
+    eps = float(getattr(q_norm, "eps", 1e-5))
+    pdt = _dt(qw) if qw is not None else _lib.GPA_DTYPE_F32
+    pos = None if positions is None else positions.reshape(T, 2).to(torch.int64).contiguous()
+    n_pos = 0 if cos_table is None else cos_table.shape[0]
+    call("gpa_qk_norm_rope", ptr(qkv), qkv.stride(0), 0, H * D, T, H, D, ptr(qw), ptr(qb), ptr(kw),
+         ptr(kb), pdt, eps, ptr(pos), ptr(cos_table), ptr(sin_table), n_pos, ptr(qkv[:, 0]),
+         ptr(qkv[:, 1]), qkv.stride(0), stream_of(qkv))
+    return qkv[:, 0], qkv[:, 1], qkv[:, 2]

@@ -11,7 +11,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .layers import Block, PatchEmbed
+from .layers import Block, LayerNorm, PatchEmbed
 
 
 class DinoVisionTransformer(nn.Module):
@@ -19,7 +19,7 @@ class DinoVisionTransformer(nn.Module):
                  num_heads=16, mlp_ratio=4.0, init_values=1.0, num_register_tokens=4,
                  interpolate_antialias=True, interpolate_offset=0.0):
         super().__init__()
-        norm_layer = partial(nn.LayerNorm, eps=1e-6)
+        norm_layer = partial(LayerNorm, eps=1e-6)
         self.embed_dim = embed_dim
         self.patch_size = patch_size
         self.num_register_tokens = num_register_tokens

@@ -10,7 +10,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .layers import Block, Mlp, SdpaAttention
+from .layers import Block, LayerNorm, Mlp, SdpaAttention
 
 
 # ---------------------------------------------------------------------------
@@ -23,8 +23,8 @@ class CameraHead(nn.Module):
         self.trunk = nn.Sequential(*[
             Block(dim_in, num_heads, mlp_ratio=mlp_ratio, init_values=init_values,
                   attn_class=SdpaAttention) for _ in range(trunk_depth)])
-        self.token_norm = nn.LayerNorm(dim_in)
-        self.trunk_norm = nn.LayerNorm(dim_in)
+        self.token_norm = LayerNorm(dim_in)
+        self.trunk_norm = LayerNorm(dim_in)
         self.empty_pose_tokens = nn.Parameter(torch.zeros(1, 1, self.target_dim))
         self.embed_pose = nn.Linear(self.target_dim, dim_in)
         self.poseLN_modulation = nn.Sequential(nn.SiLU(), nn.Linear(dim_in, 3 * dim_in, bias=True))
@@ -127,7 +127,7 @@ class DPTHead(nn.Module):
         super().__init__()
         self.patch_size = patch_size
         self.activation, self.conf_activation = activation, conf_activation
-        self.norm = nn.LayerNorm(dim_in)
+        self.norm = LayerNorm(dim_in)
         self.projects = nn.ModuleList([nn.Conv2d(dim_in, oc, 1) for oc in out_channels])
         self.resize_layers = nn.ModuleList([
             nn.ConvTranspose2d(out_channels[0], out_channels[0], 4, 4),

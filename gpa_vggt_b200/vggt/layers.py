@@ -25,6 +25,18 @@ BF16 = torch.bfloat16
 # ---------------------------------------------------------------------------
 # small layers (vggt/layers/mlp.py, layer_scale.py, patch_embed.py)
 # ---------------------------------------------------------------------------
+class LayerNorm(nn.LayerNorm):
+    """nn.LayerNorm whose CUDA bf16 path is the fused kernel (fp32 statistics,
+    bf16 result: what a bf16-autocast Linear receives from the reference's fp32
+    LayerNorm).  Other inputs (the CPU, fp32, no affine) use torch."""
+
+    def forward(self, x):
+        if (x.is_cuda and x.dtype == BF16 and self.weight is not None and self.bias is not None
+                and x.shape[-1] % 256 == 0 and x.shape[-1] <= 4096):
+            return kernels.layernorm(x, self.weight, self.bias, self.eps)
+        return super().forward(x)
+
+
 class Mlp(nn.Module):
     def __init__(self, in_features, hidden_features=None, out_features=None, act_layer=nn.GELU,
                  drop=0.0, bias=True):
@@ -91,6 +103,11 @@ class RotaryPositionEmbedding2D(nn.Module):
         self.scaling_factor = scaling_factor
         self.cache = {}
 
+    def tables(self, dim, device, n_pos=1024):
+        """fp32 cos/sin tables [n_pos, dim] as the reference computes them for
+        fp32 tokens (rope.py:92-123); rows do not depend on n_pos."""
+        return self._tables(dim, n_pos, device, torch.float32)
+
     def _tables(self, dim, n_pos, device, dtype):
         key = (dim, n_pos, str(device), dtype)
         if key not in self.cache:
@@ -132,7 +149,7 @@ class Attention(nn.Module):
     """
 
     def __init__(self, dim, num_heads=8, qkv_bias=True, proj_bias=True, attn_drop=0.0,
-                 proj_drop=0.0, norm_layer=nn.LayerNorm, qk_norm=False, fused_attn=True, rope=None,
+                 proj_drop=0.0, norm_layer=LayerNorm, qk_norm=False, fused_attn=True, rope=None,
                  patch_width=37, patch_height=28, merge_ratio=0.9):
         super().__init__()
         assert dim % num_heads == 0
@@ -157,7 +174,18 @@ class Attention(nn.Module):
     # -- helpers ------------------------------------------------------------
     def _qkv(self, x, pos):
         B, N, C = x.shape
-        qkv = self.qkv(x).reshape(B, N, 3, self.num_heads, self.head_dim)
+        H, D = self.num_heads, self.head_dim
+        qkv = self.qkv(x)
+        if (qkv.is_cuda and qkv.dtype == BF16 and D == 64 and isinstance(self.q_norm, nn.LayerNorm)
+                and (self.rope is None or pos is not None)):
+            # qk-LayerNorm + RoPE + bf16 in one pass, in place on the qkv buffer
+            cos = sin = None
+            if self.rope is not None:
+                cos, sin = self.rope.tables(D // 2, qkv.device)
+            q, k, v = kernels.qk_norm_rope(qkv.view(B * N, 3, H, D), self.q_norm, self.k_norm,
+                                           None if self.rope is None else pos, cos, sin)
+            return q.view(B, N, H, D), k.view(B, N, H, D), v.view(B, N, H, D)
+        qkv = qkv.reshape(B, N, 3, H, D)
         q, k, v = qkv.unbind(2)                      # [B, N, H, D] views
         q, k = self.q_norm(q), self.k_norm(k)
         if self.rope is not None:
@@ -267,7 +295,7 @@ class SdpaAttention(Attention):
 class Block(nn.Module):
     def __init__(self, dim, num_heads, mlp_ratio=4.0, qkv_bias=True, proj_bias=True, ffn_bias=True,
                  drop=0.0, attn_drop=0.0, init_values=None, drop_path=0.0, act_layer=nn.GELU,
-                 norm_layer=nn.LayerNorm, attn_class=Attention, ffn_layer=Mlp, qk_norm=False,
+                 norm_layer=LayerNorm, attn_class=Attention, ffn_layer=Mlp, qk_norm=False,
                  fused_attn=True, rope=None, merge_ratio=0.9):
         super().__init__()
         self.norm1 = norm_layer(dim)

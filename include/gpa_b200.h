@@ -208,6 +208,34 @@ GPA_API int gpa_lse_combine(int heads, int frames, int rows_per_frame, int head_
                     const void* ob, const int64_t* ob_strides, const float* lb,
                     const int64_t* lb_strides, void* o, const int64_t* o_strides, void* stream);
 
+/*
+ * LayerNorm of bf16 rows with fp32 statistics and a bf16 result (the norm1 /
+ * norm2 of vggt/layers/block.py:85-92 as a bf16-autocast Linear consumes it).
+ * out[r, c] = bf16((x[r, c] - mean_r) * rsqrt(var_r + eps) * w[c] + b[c]).
+ * cols % 256 == 0 and cols <= 4096; weight/bias of dtype param_dtype (f32 or bf16).
+ */
+GPA_API int gpa_layernorm_bf16(const void* x, int64_t x_stride, int rows, int cols,
+                               const void* weight, const void* bias, int param_dtype, float eps,
+                               void* out, int64_t out_stride, void* stream);
+
+/*
+ * qk-LayerNorm + 2D rotary embedding, fused (vggt/layers/attention.py:216-220
+ * with vggt/layers/rope.py:139-209).  For each token t and head h of a qkv
+ * buffer (q row at qkv + t*token_stride + q_offset + h*64, k row at k_offset):
+ * LayerNorm over the 64 features (fp32, eps, per-head weight/bias; NULL = none),
+ * then, if positions != NULL, rotation of features 0..31 by positions[t, 0] and
+ * 32..63 by positions[t, 1] with the rotate-half pairing (i, i+16) and the
+ * fp32 cos/sin tables [n_pos, 32]; the bf16 results go to q_out / k_out
+ * (+ t*out_token_stride + h*64), which may alias the q / k rows of qkv.
+ */
+GPA_API int gpa_qk_norm_rope(const void* qkv, int64_t token_stride, int64_t q_offset,
+                             int64_t k_offset, int tokens, int heads, int head_dim,
+                             const void* q_weight, const void* q_bias, const void* k_weight,
+                             const void* k_bias, int param_dtype, float eps,
+                             const int64_t* positions, const float* cos_table,
+                             const float* sin_table, int n_pos, void* q_out, void* k_out,
+                             int64_t out_token_stride, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
