@@ -12,7 +12,10 @@ from pathlib import Path
 
 import torch
 
-LIB_PATH = Path(__file__).resolve().with_name("libgpa_b200.so")
+import os
+
+# GPA_LIB_PATH points the binding at another build of the same C ABI.
+LIB_PATH = Path(os.environ.get("GPA_LIB_PATH") or Path(__file__).resolve().with_name("libgpa_b200.so"))
 
 GPA_OK = 0
 GPA_DTYPE_F32 = 0

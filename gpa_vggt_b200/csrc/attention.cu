@@ -19,9 +19,10 @@
 //               polynomial on the FMA pipe to offload the MUFU unit (16/clk/SM);
 //               scale/bias, max and sum use packed fp32x2 and 3-input max with
 //               independent accumulators.
-//   MMA order:  S_t(j+1) is issued as soon as softmax t has pulled S_t(j) into
-//               registers, before O_t += P_t(j) V_j, so a softmax warpgroup finds
-//               its next score tile ready when it finishes the current one.
+//   MMA order:  out of order across the two tiles: S_t(j+1) is issued as soon
+//               as softmax t has pulled S_t(j) into registers, O_t += P_t(j) V_j
+//               as soon as P_t(j) is in TMEM, whichever comes first, so neither
+//               softmax warpgroup waits on the other's progress.
 //   TMEM (512 columns): S0 0..127, S1 128..255, O0 256..319, O1 320..383,
 //                       P0 384..447, P1 448..511 (P: two bf16 per column).
 //   The producer/MMA warpgroup gives registers to the softmax warpgroups
@@ -40,7 +41,11 @@ constexpr int TILE_BYTES = BM * HD * 2;  // 16 KB
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 constexpr int THREADS = 384;
 constexpr int TMEM_COLS = 512;
-constexpr int REGS_LOW = 56, REGS_HIGH = 216, REGS_LAUNCH = 168;
+#ifndef GPA_ATTN_REGS_LOW
+#define GPA_ATTN_REGS_LOW 56
+#endif
+constexpr int REGS_LOW = GPA_ATTN_REGS_LOW, REGS_HIGH = (168 * 384 - GPA_ATTN_REGS_LOW * 128) / 256 / 8 * 8,
+              REGS_LAUNCH = 168;
 static_assert(REGS_LOW * 128 + REGS_HIGH * 256 <= REGS_LAUNCH * THREADS, "register split");
 
 struct Smem {
@@ -65,12 +70,24 @@ struct Params {
   int* status;
 };
 
-// exponentials of one group of 8 shifted scores: elements 5..7 on the FMA pipe
+// How many of each group of 8 exponentials run as the FMA-pipe polynomial
+// (the rest on MUFU, 16/clk/SM); 3 balances MUFU against issue slots.
+#ifndef GPA_ATTN_POLY_PER8
+#define GPA_ATTN_POLY_PER8 3
+#endif
+constexpr int kPolyPer8 = GPA_ATTN_POLY_PER8;
+// 1: compute a tile's exponentials before its row sums / packing
+#ifndef GPA_ATTN_EXP_FIRST
+#define GPA_ATTN_EXP_FIRST 0
+#endif
+
+// exponentials of one group of 8 shifted scores: the last kPolyPer8 on the FMA pipe
 __device__ __forceinline__ void exp8(const float* x, float* e) {
 #pragma unroll
-  for (int i = 0; i < 5; ++i) e[i] = fast_exp2(x[i]);
-  exp2_poly2(x[5], x[6], e[5], e[6]);
-  e[7] = exp2_poly(x[7]);
+  for (int i = 0; i < 8 - kPolyPer8; ++i) e[i] = fast_exp2(x[i]);
+#pragma unroll
+  for (int i = 8 - kPolyPer8; i + 1 < 8; i += 2) exp2_poly2(x[i], x[i + 1], e[i], e[i + 1]);
+  if (kPolyPer8 & 1) e[7] = exp2_poly(x[7]);
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -200,27 +217,47 @@ __global__ void __launch_bounds__(THREADS, 1)
           issue_s(0, 0);
           issue_s(1, 0);
         }
-        for (int j = 0; okw && j < nk; ++j) {
-          if (j + 1 < nk) {  // next score tiles, as soon as the softmax holds S(j)
-            if (!(okw = wait_bar(&kv_full[(j + 1) % STAGES], ((j + 1) / STAGES) & 1, abort_flag,
-                                 p.status, kDevTimeout)))
-              break;
-#pragma unroll
-            for (int t = 0; t < 2; ++t) {
-              if (!(okw = wait_bar(&s_empty[t], j & 1, abort_flag, p.status, kDevTimeout))) break;
-              tc_fence_after();
-              issue_s(t, j + 1);
-            }
-            if (!okw) break;
-          }
+        // Issue whatever is ready, per query tile t: S_t(j) once softmax t holds
+        // S_t(j-1) and K_j has landed; O_t += P_t(j) V_j once P_t(j) is written.
+        // A K/V stage is released after both tiles' PV of that key tile.
+        int s_next[2] = {1, 1}, pv_next[2] = {0, 0}, released = 0;
+        unsigned long long idle_since = 0;
+        while (okw && (pv_next[0] < nk || pv_next[1] < nk)) {
+          bool progressed = false;
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
-            if (!(okw = wait_bar(&p_full[t], j & 1, abort_flag, p.status, kDevTimeout))) break;
-            tc_fence_after();
-            issue_o(t, j);
+            const int js = s_next[t];
+            if (js < nk && bar_try_wait(&s_empty[t], (js - 1) & 1) &&
+                bar_try_wait(&kv_full[js % STAGES], (js / STAGES) & 1)) {
+              tc_fence_after();
+              issue_s(t, js);
+              s_next[t] = js + 1;
+              progressed = true;
+            }
+            const int jp = pv_next[t];
+            if (jp < nk && bar_try_wait(&p_full[t], jp & 1)) {
+              tc_fence_after();
+              issue_o(t, jp);
+              pv_next[t] = jp + 1;
+              progressed = true;
+            }
           }
-          if (!okw) break;
-          umma_commit(&kv_empty[j % STAGES]);
+          const int both = min(pv_next[0], pv_next[1]);
+          while (released < both) {
+            umma_commit(&kv_empty[released % STAGES]);
+            ++released;
+          }
+          if (progressed) {
+            idle_since = 0;
+          } else if (idle_since == 0) {
+            idle_since = global_ns();
+          } else if (*abort_flag) {
+            okw = false;
+          } else if (global_ns() - idle_since > kWaitLimitNs) {
+            *abort_flag = 1;
+            if (p.status) atomicExch(p.status, kDevTimeout);
+            okw = false;
+          }
         }
       }
     }
@@ -272,33 +309,49 @@ __global__ void __launch_bounds__(THREADS, 1)
         l *= alpha;
         m_ref = mt;
       }
-      // P_t and O_t are free once the previous O_t += P_t V finished
-      if (j > 0) {
-        okw = wait_bar(&o_done[t], (j - 1) & 1, abort_flag, p.status, kDevTimeout);
-        if (!__all_sync(0xffffffffu, okw)) { okw = false; break; }
-        tc_fence_after();
-      }
       float acc[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = 0.f;
       const float neg_m = -m_ref;
+#if GPA_ATTN_EXP_FIRST
+      // all exponentials first (independent streams for the scheduler), in place
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {  // 64 keys -> 32 packed columns per half
-        uint32_t pk[32];
+      for (int g = 0; g < 16; ++g) {
+        float* xg = x + g * 8;
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          float* xg = x + hf * 64 + g * 8;
+        for (int i = 0; i < 8; i += 2) fadd2(xg[i], xg[i + 1], xg[i], xg[i + 1], neg_m, neg_m);
+        exp8(xg, xg);
+      }
+#endif
+#pragma unroll
+      for (int qt = 0; qt < 4; ++qt) {  // 32 keys -> 16 packed bf16 pairs per quarter
+        uint32_t pk[16];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          float* xg = x + qt * 32 + g * 8;
+#if GPA_ATTN_EXP_FIRST
+          const float* e = xg;
+#else
 #pragma unroll
           for (int i = 0; i < 8; i += 2) fadd2(xg[i], xg[i + 1], xg[i], xg[i + 1], neg_m, neg_m);
           float e[8];
           exp8(xg, e);
+#endif
 #pragma unroll
           for (int i = 0; i < 8; i += 2) fadd2(acc[i], acc[i + 1], acc[i], acc[i + 1], e[i], e[i + 1]);
 #pragma unroll
           for (int i = 0; i < 4; ++i) pk[g * 4 + i] = pack_bf16x2(e[2 * i], e[2 * i + 1]);
         }
-        tmem_st32(tP + hf * 32, pk);
+        // P_t and O_t are free once the previous O_t += P_t V finished; the
+        // first quarter of the exponentials hides that wait
+        if (qt == 0 && j > 0) {
+          okw = wait_bar(&o_done[t], (j - 1) & 1, abort_flag, p.status, kDevTimeout);
+          if (!__all_sync(0xffffffffu, okw)) { okw = false; break; }
+          tc_fence_after();
+        }
+        tmem_st16(tP + qt * 16, pk);
       }
+      if (!okw) break;
       l += ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
       // rescale O_t in TMEM where the running max moved
       if (j > 0 && __any_sync(0xffffffffu, moved)) {
