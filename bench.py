@@ -17,10 +17,13 @@ Workload "merged_block": one merged global block's attention core at S frames
 (roles, projection, similarity argmax, plan, K/V scatter-mean, biased
 attention).
 
-With N > 1 (torchrun) each rank runs its own replica (weak scaling) until the
-query-frame sharding lands.  --impl reference times the reference's CPU path
-(the oracle port in oracle/, torch on all host cores) on a bounded sample and
-extrapolates it to the same workload.
+With N > 1 (torchrun, one process per GPU, NCCL) the forward's S frames are
+sharded by query frame (gpa_vggt_b200/vggt/shard.py): each rank runs S/N
+frames end to end and the global blocks all-gather what their keys need
+(strong scaling; the time is the max over ranks).  The merged_block workload
+runs one replica per rank (weak scaling).  --impl reference times the
+reference's CPU path (the oracle port in oracle/, torch on all host cores) on
+a bounded sample and extrapolates it to the same workload.
 """
 from __future__ import annotations
 
@@ -137,7 +140,7 @@ def forward(model, images):
     import torch
     with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
         taps, psi = model.aggregator(images)
-        pose = model.camera_head(taps)[-1]
+        pose = model.camera_head(taps, shard=model.aggregator.shard)[-1]
         depth, conf = model.depth_head(taps, images=images, patch_start_idx=psi)
     return pose, depth, conf
 
@@ -295,9 +298,15 @@ def main():
                   "merge_ratio": args.ratio, "heads": 16, "head_dim": 64,
                   "l2": "inputs > L2 (no flush needed)"}
         metric = f"GPA merged global block latency (ms) at S={S}"
-    config["parallelism"] = f"replicas x{world}" if world > 1 else "single GPU"
+    if world == 1:
+        config["parallelism"] = "single GPU"
+    elif fwd:
+        config["parallelism"] = f"query-frame shards x{world} (NCCL all-gather of keys per global block)"
+    else:
+        config["parallelism"] = f"replicas x{world}"
     base = {"metric": metric, "unit": "ms", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "higher_is_better": False, "scaling": "weak",
+            "warmup": args.warmup, "higher_is_better": False,
+            "scaling": "strong" if (fwd and world > 1) else "weak",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (torch.rand frames / seeded N(0,1) tokens, random-init weights)",
             "config": config}
@@ -341,7 +350,15 @@ def main():
     if fwd:
         model = build_model(dev, args.vanilla)
         g = torch.Generator(device="cpu").manual_seed(0)
-        images = torch.rand(1, S, 3, 518, 518, generator=g).to(torch.bfloat16).to(dev)
+        images = torch.rand(1, S, 3, 518, 518, generator=g).to(torch.bfloat16)
+        S_local = S
+        if world > 1:
+            from gpa_vggt_b200.vggt.shard import FrameShard
+            shard = FrameShard(S)
+            model.set_shard(shard)
+            images = images[:, shard.f0:shard.f1]
+            S_local = shard.local
+        images = images.contiguous().to(dev)
         step = lambda: forward(model, images)  # noqa: E731
     else:
         x, qkv = make_block_inputs(S, dev, seed=rank)
@@ -378,8 +395,8 @@ def main():
         if fwd:
             h_img = images.cpu().pin_memory()
             h_pose = torch.empty(1, S, 9, dtype=torch.float32).pin_memory()
-            h_depth = torch.empty(1, S, 518, 518, 1, dtype=torch.float32).pin_memory()
-            h_conf = torch.empty(1, S, 518, 518, dtype=torch.float32).pin_memory()
+            h_depth = torch.empty(1, S_local, 518, 518, 1, dtype=torch.float32).pin_memory()
+            h_conf = torch.empty(1, S_local, 518, 518, dtype=torch.float32).pin_memory()
 
             def e2e_step():
                 d_img = h_img.to(dev, non_blocking=True)
@@ -426,7 +443,7 @@ def main():
             e_ms = t.item()
         e2e = {"value": e_ms, "unit": "ms", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
         if fwd:
-            e2e["frames_per_s"] = world * S / (e_ms / 1e3)
+            e2e["frames_per_s"] = S / (e_ms / 1e3)   # the job covers S frames at any N
 
     pk = peaks()
     achieved = attn_flops / (attn_ms * 1e-3) / 1e12
@@ -439,7 +456,7 @@ def main():
     line = dict(base, value=ms, ms_per_step=ms, gpu_launches=launches, roofline=roof, e2e=e2e,
                 clocks=clk.summary())
     if fwd:
-        line["frames_per_s"] = world * S / (ms / 1e3)
+        line["frames_per_s"] = S / (ms / 1e3)
         line["gpu_memory_peak_gib"] = torch.cuda.max_memory_allocated(dev) / 2 ** 30
     if rank == 0 and not args.no_cpu:
         if fwd:

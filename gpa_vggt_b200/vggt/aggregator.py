@@ -26,8 +26,11 @@ def merge_window(block_num, merging, merge_end, early_frame_split, core_blocks, 
             and (block_num not in core_blocks or core_merge_ratio > 0))
 
 
-def special_tokens(token, B, S):
-    """[1, 2, X, C] -> [B*S, X, C]: slot 0 for frame 0, slot 1 for the others."""
+def special_tokens(token, B, S, first_frame=0):
+    """[1, 2, X, C] -> [B*S, X, C] for frames first_frame.. first_frame+S-1:
+    slot 0 for (global) frame 0, slot 1 for the others."""
+    if first_frame > 0:
+        return token[:, 1:].expand(B, S, *token.shape[2:]).reshape(B * S, *token.shape[2:])
     first = token[:, 0:1].expand(B, 1, *token.shape[2:])
     rest = token[:, 1:].expand(B, S - 1, *token.shape[2:])
     return torch.cat([first, rest], 1).reshape(B * S, *token.shape[2:])
@@ -69,10 +72,19 @@ class Aggregator(nn.Module):
         self.camera_token = nn.Parameter(torch.randn(1, 2, 1, embed_dim))
         self.register_token = nn.Parameter(torch.randn(1, 2, num_register_tokens, embed_dim))
         self.patch_start_idx = 1 + num_register_tokens
+        self.shard = None
+        self.tap_blocks = (4, 11, 17, 23)   # block outputs the DPT head reads (aggregator.py:296)
         self.register_buffer("_resnet_mean", torch.tensor(_RESNET_MEAN).view(1, 1, 3, 1, 1),
                              persistent=False)
         self.register_buffer("_resnet_std", torch.tensor(_RESNET_STD).view(1, 1, 3, 1, 1),
                              persistent=False)
+
+    def set_shard(self, shard):
+        """Run the global blocks with their queries sharded by frame (shard.py);
+        forward() then receives only this rank's frames."""
+        self.shard = shard
+        for blk in self.global_blocks:
+            blk.attn.shard = shard
 
     def set_patch_dims(self, pw, ph):
         for m in self.modules():
@@ -85,8 +97,9 @@ class Aggregator(nn.Module):
         dt = self.camera_token.dtype
         x = ((images - self._resnet_mean) / self._resnet_std).to(dt).view(B * S, 3, H, W)
         patch = self.patch_embed(x).to(dt)
-        tokens = torch.cat([special_tokens(self.camera_token, B, S),
-                            special_tokens(self.register_token, B, S), patch], 1).to(dt)
+        f0 = self.shard.f0 if self.shard is not None else 0
+        tokens = torch.cat([special_tokens(self.camera_token, B, S, f0),
+                            special_tokens(self.register_token, B, S, f0), patch], 1).to(dt)
         pos = self.position_getter(B * S, H // self.patch_size, W // self.patch_size, images.device) + 1
         pos = torch.cat([torch.zeros(B * S, self.patch_start_idx, 2, device=images.device,
                                      dtype=pos.dtype), pos], 1)
@@ -99,6 +112,6 @@ class Aggregator(nn.Module):
                                    self.core_blocks, self.core_merge_ratio) else None
             tokens = self.global_blocks[b](tokens.view(B, S * P, C), pos=pos.view(B, S * P, 2),
                                            global_merging=gm)
-            if b in (4, 11, 17, 23):
+            if b in self.tap_blocks:
                 taps.append(torch.cat([frame_out, tokens.view(B, S, P, C)], -1))
         return taps, self.patch_start_idx

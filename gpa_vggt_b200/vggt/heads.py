@@ -31,8 +31,11 @@ class CameraHead(nn.Module):
         self.adaln_norm = nn.LayerNorm(dim_in, elementwise_affine=False, eps=1e-6)
         self.pose_branch = Mlp(dim_in, dim_in // 2, self.target_dim)
 
-    def forward(self, taps: List[torch.Tensor], num_iterations: int = 4) -> List[torch.Tensor]:
-        pose_tokens = self.token_norm(taps[-1][:, :, 0])          # [B, S, 2C]
+    def forward(self, taps: List[torch.Tensor], num_iterations: int = 4, shard=None) -> List[torch.Tensor]:
+        cam = taps[-1][:, :, 0]                                   # [B, S, 2C] camera tokens
+        if shard is not None and shard.active:                    # every frame's camera token
+            cam = shard.gather(cam[0].contiguous())[None]
+        pose_tokens = self.token_norm(cam)
         B, S, C = pose_tokens.shape
         pred, out = None, []
         for _ in range(num_iterations):

@@ -17,7 +17,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .. import kernels
-from ..merging.merge import build_plan
+from ..merging.merge import build_plan, draw_dst_choice, projection_basis
 
 BF16 = torch.bfloat16
 
@@ -165,6 +165,7 @@ class Attention(nn.Module):
         self.merge_grid = 2
         self.merge_metric_dim = 0
         self.rng_override = None
+        self.shard = None            # FrameShard of a global block run across GPUs
         self.qkv = nn.Linear(dim, dim * 3, bias=qkv_bias)
         self.q_norm = norm_layer(self.head_dim) if qk_norm else nn.Identity()
         self.k_norm = norm_layer(self.head_dim) if qk_norm else nn.Identity()
@@ -206,9 +207,71 @@ class Attention(nn.Module):
             out = merged_attention(x, q, k, v, self)
         else:
             out = torch.empty(B, N, self.num_heads, self.head_dim, device=x.device, dtype=BF16)
-            kernels.attention(self._heads(q.to(BF16)), self._heads(k.to(BF16)),
-                              self._heads(v.to(BF16)), None, self.scale, out=self._heads(out))
+            k, v = k.to(BF16), v.to(BF16)
+            if self.shard is not None and self.shard.active:   # keys of every frame
+                k = self.shard.gather(k[0].contiguous())[None]
+                v = self.shard.gather(v[0].contiguous())[None]
+            kernels.attention(self._heads(q.to(BF16)), self._heads(k), self._heads(v), None,
+                              self.scale, out=self._heads(out))
         return self.proj(out.reshape(B, N, C))
+
+
+def _merge_draws(attn: Attention, num_imgs: int, C: int, device, dtype):
+    """The two random draws of a merge: dst pick per window and projection basis
+    (injected by tests, else drawn as the reference draws them)."""
+    if attn.rng_override is not None:
+        return attn.rng_override
+    gen = torch.Generator(device=device)
+    gen.manual_seed(33)
+    rand_idx = draw_dst_choice(num_imgs, attn.patch_width, attn.patch_height, attn.merge_grid,
+                               attn.merge_grid, device, gen)
+    proj = projection_basis(C, attn.merge_metric_dim, device, dtype) if attn.merge_metric_dim else None
+    return rand_idx, proj
+
+
+def merged_attention_sharded(x, q, k, v, attn: Attention) -> torch.Tensor:
+    """Merged block with the queries sharded by frame (see shard.py): every rank
+    builds the same global plan from all-gathered match results and merges the
+    all-gathered K/V; attention runs for the rank's own queries only."""
+    sh = attn.shard
+    B, Nl, C = x.shape
+    H, D = attn.num_heads, attn.head_dim
+    pw, ph, ns, g = attn.patch_width, attn.patch_height, attn.num_special, attn.merge_grid
+    P = pw * ph + ns
+    S, N = sh.frames, sh.frames * P
+    if Nl != sh.local * P:
+        raise ValueError("merged_attention_sharded: local tokens do not match the frame shard")
+    dev = x.device
+    rand_idx, proj = _merge_draws(attn, S, C, dev, x.dtype)
+    dst_pos, src_pos, _ = kernels.merge_roles(rand_idx, S, pw, ph, g, g, ns, False, dev)
+    dpf = ns + (ph // g) * (pw // g)
+    ranges = sh.role_ranges(P, dpf)
+    (d0, d1), (s0, s1) = ranges[sh.rank]
+    base = sh.f0 * P
+    metric = x[0]
+    if attn.merge_metric_dim and attn.merge_metric_dim < C:
+        metric = metric @ proj.to(metric.dtype)
+    a, b = kernels.metric_split(metric, src_pos[s0:s1] - base, dst_pos[d0:d1] - base)
+    b_full = sh.gather_varlen(b, [rd[1] - rd[0] for rd, _ in ranges])
+    if s1 > s0:
+        nm, ni = kernels.sim_argmax(a[None], b_full[None])
+        nm, ni = nm[0], ni[0]
+    else:
+        nm = torch.empty(0, device=dev)
+        ni = torch.empty(0, device=dev, dtype=torch.int32)
+    src_counts = [rs[1] - rs[0] for _, rs in ranges]
+    nm_full = sh.gather_varlen(nm, src_counts)
+    ni_full = sh.gather_varlen(ni, src_counts)
+    plan = kernels.merge_plan(nm_full, ni_full, int(N * attn.merge_ratio), dst_pos, src_pos)
+    k_full = sh.gather(k[0].contiguous())                       # [N, H, D]
+    v_full = sh.gather(v[0].contiguous())
+    km = kernels.merge_kv(k_full.transpose(0, 1), plan)
+    vm = kernels.merge_kv(v_full.transpose(0, 1), plan)
+    bias = plan.counts.log().to(BF16).float()
+    out = torch.empty(1, Nl, H, D, device=dev, dtype=BF16)
+    kernels.attention(q.to(BF16).permute(0, 2, 1, 3), km.to(BF16)[None], vm.to(BF16)[None],
+                      bias[None, None], attn.scale, out=out.permute(0, 2, 1, 3))
+    return out
 
 
 def merged_attention(x, q, k, v, attn: Attention) -> torch.Tensor:
@@ -218,6 +281,8 @@ def merged_attention(x, q, k, v, attn: Attention) -> torch.Tensor:
     H, D = attn.num_heads, attn.head_dim
     if B != 1:
         raise NotImplementedError("merged_attention: batch size 1 (the reference's eval setting)")
+    if attn.shard is not None and attn.shard.active:
+        return merged_attention_sharded(x, q, k, v, attn)
     r = int(N * attn.merge_ratio)
     rand_idx = proj = None
     gen = None
@@ -250,7 +315,8 @@ def frame_special_attention(q, k, v, attn: Attention) -> torch.Tensor:
         raise NotImplementedError("frame_special_attention: batch size 1")
     pts, pw, ph, kp = attn.num_special, attn.patch_width, attn.patch_height, attn.broadcast_pool
     P = pw * ph + pts
-    S = N // P
+    S = N // P                      # this rank's frames
+    sh = attn.shard if (attn.shard is not None and attn.shard.active) else None
     if S * P != N:
         raise ValueError(f"frame_special: token count {N} is not S*(patch_w*patch_h+{pts})")
     if kp <= 0:
@@ -264,9 +330,20 @@ def frame_special_attention(q, k, v, attn: Attention) -> torch.Tensor:
     # (b) shared set: specials of every frame, then the pooled summaries
     kh, vh = k[0].transpose(0, 1), v[0].transpose(0, 1)       # [H, N, D] views
     pk, pv, size = kernels.frame_pool(kh, vh, S, ph, pw, pts, kp)
-    sk = torch.cat([k5[:, :pts].permute(2, 0, 1, 3).reshape(H, S * pts, D), pk], 1)
-    sv = torch.cat([v5[:, :pts].permute(2, 0, 1, 3).reshape(H, S * pts, D), pv], 1)
-    bias = torch.cat([torch.zeros(H, S * pts, device=q.device), size.log()], 1)
+    spk, spv = k5[:, :pts], v5[:, :pts]                       # [S, pts, H, D]
+    St = S
+    if sh is not None:                 # the shared set of every frame
+        npool = pk.shape[1] // S
+        St = sh.frames
+        spk, spv = sh.gather(spk.contiguous()), sh.gather(spv.contiguous())
+        pk = sh.gather(pk.view(H, S, npool, D).transpose(0, 1).contiguous()).transpose(0, 1)
+        pv = sh.gather(pv.view(H, S, npool, D).transpose(0, 1).contiguous()).transpose(0, 1)
+        pk, pv = pk.reshape(H, St * npool, D), pv.reshape(H, St * npool, D)
+        size = sh.gather(size.view(H, S, npool).transpose(0, 1).contiguous()).transpose(0, 1)
+        size = size.reshape(H, St * npool)
+    sk = torch.cat([spk.permute(2, 0, 1, 3).reshape(H, St * pts, D), pk], 1)
+    sv = torch.cat([spv.permute(2, 0, 1, 3).reshape(H, St * pts, D), pv], 1)
+    bias = torch.cat([torch.zeros(H, St * pts, device=q.device), size.log()], 1)
     bias = bias.to(BF16).float()                               # the reference casts it to bf16
     out_b, lse_b = kernels.attention(q[0].transpose(0, 1)[None], sk[None], sv[None], bias[None],
                                      attn.scale, return_lse=True)

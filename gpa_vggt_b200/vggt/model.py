@@ -28,13 +28,19 @@ class VGGT(nn.Module):
     def update_patch_dimensions(self, patch_width: int, patch_height: int):
         self.aggregator.set_patch_dims(patch_width, patch_height)
 
+    def set_shard(self, shard):
+        """Shard the frames across the ranks of shard.group (see shard.py):
+        forward() takes this rank's frames and returns their depth, and the
+        camera encoding of every frame."""
+        self.aggregator.set_shard(shard)
+
     def forward(self, images: torch.Tensor):
         if images.dim() == 4:
             images = images[None]
         taps, psi = self.aggregator(images)
         out = {}
         if self.camera_head is not None:
-            poses = self.camera_head(taps)
+            poses = self.camera_head(taps, shard=self.aggregator.shard)
             out["pose_enc"] = poses[-1]
             out["pose_enc_list"] = poses
         if self.depth_head is not None:

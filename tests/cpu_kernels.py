@@ -1,0 +1,93 @@
+"""CPU stand-ins for the kernel entry points of gpa_vggt_b200.kernels, built on
+the oracle -- test infrastructure for exercising the host logic (model wiring,
+frame sharding) on CPU.  install(monkeypatch_like) swaps them in."""
+from types import SimpleNamespace
+
+import torch
+
+from oracle import gpa_oracle as O
+
+
+def attention(q, k, v, bias, sm_scale, return_lse=False, out=None, status=None):
+    b = None if bias is None else bias.reshape(bias.shape[0], bias.shape[1], 1, -1)
+    res = O.attention_keybias(q, k, v, b, sm_scale, return_lse=True)
+    o, lse = res[0].to(q.dtype), res[1].float()
+    if out is not None:
+        out.copy_(o)
+        o = out
+    return (o, lse) if return_lse else o
+
+
+def merge_roles(rand_idx, num_imgs, w, h, sx, sy, num_special, no_rand, device):
+    mask = O.dst_mask(num_imgs, w, h, sx, sy, num_special,
+                      None if rand_idx is None else rand_idx.cpu(), no_rand)
+    dst, src = O.split_positions(mask)
+    slot = torch.empty(mask.numel(), dtype=torch.int32)
+    slot[dst] = torch.arange(dst.numel(), dtype=torch.int32)
+    slot[src] = -torch.arange(src.numel(), dtype=torch.int32) - 1
+    return dst.int(), src.int(), slot
+
+
+def metric_split(metric, src_pos, dst_pos):
+    m = O.normalize_rows(metric.float())
+    return m[src_pos.long()].to(torch.bfloat16), m[dst_pos.long()].to(torch.bfloat16)
+
+
+def sim_argmax(a, b, status=None):
+    nms, nis = [], []
+    for i in range(a.shape[0]):
+        nm, ni, _ = O.sim_argmax(a[i], b[i])
+        nms.append(nm.float())
+        nis.append(ni.int())
+    return torch.stack(nms), torch.stack(nis)
+
+
+def merge_plan(node_max, node_idx, r, dst_pos, src_pos):
+    ns, nd = src_pos.numel(), dst_pos.numel()
+    plan = O.merge_plan(node_max.double(), node_idx.long(), r, nd)
+    return SimpleNamespace(oracle=plan, dst=dst_pos.long(), src=src_pos.long(),
+                           counts=plan.counts.float(), n_out=plan.unm_len + nd)
+
+
+def merge_kv(t, plan, mean=True, out=None, log_counts=None):
+    res = O.merge_heads(t, plan.oracle, plan.dst, plan.src, "mean" if mean else "sum").to(t.dtype)
+    if out is not None:
+        out.copy_(res)
+        return out
+    return res
+
+
+def frame_pool(k, v, S, ph, pw, pts, kp):
+    H, N, D = k.shape
+    P = ph * pw + pts
+    pk, pv, size, _ = O.frame_pool(k.reshape(H, S, P, D), v.reshape(H, S, P, D), ph, pw, pts, kp)
+    return pk.to(k.dtype), pv.to(k.dtype), size
+
+
+def lse_combine(oa, la, ob, lb, out=None):
+    res = O.lse_combine(oa, la.double(), ob, lb.double()).to(oa.dtype)
+    out.copy_(res)
+    return out
+
+
+def build_plan(metric, w, h, sx, sy, r, no_rand=False, generator=None, metric_dim=0,
+               num_special=5, rand_idx=None, proj=None):
+    N = metric.shape[0]
+    S = N // (w * h + num_special)
+    dst, src, _ = merge_roles(rand_idx, S, w, h, sx, sy, num_special, no_rand, metric.device)
+    m = O.project_metric(metric.float(), proj.float(), autocast_bf16=False) if proj is not None else metric
+    m = O.normalize_rows(m.float())
+    nm, ni, _ = O.sim_argmax(m[src.long()], m[dst.long()])
+    return merge_plan(nm, ni, r, dst, src)
+
+
+def install(setattr_fn, fp32=True):
+    """Swap the stand-ins into the kernel module (setattr_fn(obj, name, value))."""
+    from gpa_vggt_b200 import kernels
+    from gpa_vggt_b200.vggt import layers
+    for name in ("attention", "merge_roles", "metric_split", "sim_argmax", "merge_plan", "merge_kv",
+                 "frame_pool", "lse_combine"):
+        setattr_fn(kernels, name, globals()[name])
+    setattr_fn(layers, "build_plan", build_plan)
+    if fp32:
+        setattr_fn(layers, "BF16", torch.float32)

@@ -1,0 +1,111 @@
+"""Query-frame sharding (gpa_vggt_b200/vggt/shard.py), checked on CPU with two
+gloo ranks: a small VGGT (dim 128, 4 global blocks covering frame+shared,
+merged and core-merged attention, 9x9 patch grid) run with its frames split
+over the ranks must give the unsharded run's tokens and camera encoding.  The
+kernel entry points are the oracle-backed CPU stand-ins (tests/cpu_kernels.py),
+so the check is on the host logic: roles, gathers, plan, ordering."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+S, IMG = 4, 126          # 4 frames of 126x126 -> 9x9 patches
+OUT = "shard_out_rank{}.pt"
+
+
+def _model():
+    from gpa_vggt_b200.vggt.model import VGGT, init_weights
+    m = VGGT(img_size=518, embed_dim=128, merging=2, merge_end=3, merge_ratio=0.9,
+             early_frame_split=1, broadcast_pool=4, core_blocks=(3,), core_merge_ratio=0.3,
+             merge_metric_dim=64, enable_depth=False)
+    agg = m.aggregator
+    agg.depth = 4
+    agg.tap_blocks = (0, 1, 2, 3)
+    agg.frame_blocks = agg.frame_blocks[:4]
+    agg.global_blocks = agg.global_blocks[:4]
+    agg.patch_embed.blocks = agg.patch_embed.blocks[:2]
+    init_weights(m, seed=1)
+    m.eval()
+    m.update_patch_dimensions(9, 9)
+    return m
+
+
+def _draws(C=128, dim=64):
+    g = torch.Generator().manual_seed(33)
+    rand_idx = torch.randint(4, size=(S - 1, 4, 4), generator=g)
+    proj = torch.randn(C, dim, generator=torch.Generator().manual_seed(1234))
+    return rand_idx, proj
+
+
+def _run(model, images):
+    with torch.no_grad():
+        taps, _ = model.aggregator(images)
+        pose = model.camera_head(taps, shard=model.aggregator.shard)[-1]
+    return taps[-1], pose
+
+
+class _Patch:
+    def __init__(self):
+        self.saved = []
+
+    def __call__(self, obj, name, value):
+        self.saved.append((obj, name, getattr(obj, name)))
+        setattr(obj, name, value)
+
+    def undo(self):
+        for obj, name, value in reversed(self.saved):
+            setattr(obj, name, value)
+
+
+def _worker(rank, world, port, tmpdir):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import cpu_kernels
+    from gpa_vggt_b200.vggt.shard import FrameShard
+    cpu_kernels.install(setattr)
+    model = _model()
+    shard = FrameShard(S)
+    model.set_shard(shard)
+    for blk in model.aggregator.global_blocks:
+        blk.attn.rng_override = _draws()
+    images = torch.rand(1, S, 3, IMG, IMG, generator=torch.Generator().manual_seed(0))
+    tap, pose = _run(model, images[:, shard.f0:shard.f1])
+    torch.save({"tap": tap, "pose": pose, "f0": shard.f0, "f1": shard.f1},
+               os.path.join(tmpdir, OUT.format(rank)))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_frame_sharded_forward_matches_unsharded(tmp_path):
+    import cpu_kernels
+    patch = _Patch()
+    cpu_kernels.install(patch)
+    try:
+        model = _model()
+        for blk in model.aggregator.global_blocks:
+            blk.attn.rng_override = _draws()
+        images = torch.rand(1, S, 3, IMG, IMG, generator=torch.Generator().manual_seed(0))
+        ref_tap, ref_pose = _run(model, images)
+    finally:
+        patch.undo()
+    world = 2
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       start_method="spawn")
+    for r in range(world):
+        got = torch.load(tmp_path / OUT.format(r))
+        want = ref_tap[:, got["f0"]:got["f1"]]
+        assert torch.allclose(got["tap"], want, atol=1e-4, rtol=1e-4), \
+            float((got["tap"] - want).abs().max())
+        assert torch.allclose(got["pose"], ref_pose, atol=1e-4, rtol=1e-4)
