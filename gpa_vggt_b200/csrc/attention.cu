@@ -48,19 +48,33 @@ constexpr int REGS_LOW = GPA_ATTN_REGS_LOW, REGS_HIGH = (168 * 384 - GPA_ATTN_RE
               REGS_LAUNCH = 168;
 static_assert(REGS_LOW * 128 + REGS_HIGH * 256 <= REGS_LAUNCH * THREADS, "register split");
 
+// Per-key bias as one more K=16 step of S = Q K^T: A_x = [1, 1, 0..] per query
+// row, B_x = [hi(beta_j), lo(beta_j), 0..] per key with beta_j = bias_j / scale
+// split into two bf16s (about 16 bits), so S' = q.k + beta and
+// scale*log2e*S' = q.k*scale*log2e + bias*log2e.  128 x 16 bf16, K-major, no
+// swizzle: 8x8 core matrices, rows 16 B apart, K halves LBO=128 B apart, row
+// groups SBO=256 B apart.
+constexpr int XTILE_BYTES = BM * 16 * 2;  // 4 KB
+__host__ __device__ constexpr int xtile_off(int row, int k) {
+  return (row >> 3) * 256 + (k >> 3) * 128 + (row & 7) * 16 + (k & 7) * 2;
+}
+constexpr float kMaskedBeta = -1.0e30f;   // keys past n
+
 struct Smem {
   static constexpr int Q = 0;                               // 2 x 16 KB
   static constexpr int K = Q + 2 * TILE_BYTES;              // STAGES x 16 KB
   static constexpr int V = K + STAGES * TILE_BYTES;         // STAGES x 16 KB
-  static constexpr int BIAS = V + STAGES * TILE_BYTES;      // STAGES x 512 B
-  static constexpr int BARS = BIAS + STAGES * BN * 4;
+  static constexpr int ONES = V + STAGES * TILE_BYTES;      // 4 KB
+  static constexpr int BIAS = ONES + XTILE_BYTES;           // STAGES x 4 KB
+  static constexpr int BARS = BIAS + STAGES * XTILE_BYTES;
   static constexpr int TOTAL = BARS + 256;
   static constexpr int ALLOC = TOTAL + 1024;
 };
 
 struct Params {
   int m, n, heads;
-  float scale_log2;
+  float scale;        // sm_scale
+  float scale_log2;   // sm_scale * log2(e)
   const float* bias;
   int64_t bias_sb, bias_sh;
   __nv_bfloat16* o;
@@ -76,10 +90,17 @@ struct Params {
 #define GPA_ATTN_POLY_PER8 3
 #endif
 constexpr int kPolyPer8 = GPA_ATTN_POLY_PER8;
-// 1: compute a tile's exponentials before its row sums / packing
-#ifndef GPA_ATTN_EXP_FIRST
-#define GPA_ATTN_EXP_FIRST 0
-#endif
+
+
+// no-swizzle K-major descriptor of an extra-step tile
+__device__ __forceinline__ uint64_t sdesc_none(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(128 >> 4) << 16;   // LBO: next 8 K-elements
+  d |= static_cast<uint64_t>(256 >> 4) << 32;   // SBO: next 8 rows
+  d |= static_cast<uint64_t>(1) << 46;          // version; layout type 0 = no swizzle
+  return d;
+}
 
 // exponentials of one group of 8 shifted scores: the last kPolyPer8 on the FMA pipe
 __device__ __forceinline__ void exp8(const float* x, float* e) {
@@ -105,7 +126,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* o_done = p_full + 2;           // 2
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* sbias = reinterpret_cast<float*>(smem + Smem::BIAS);
 
   const int warp = warp_id(), lane = lane_id();
   const int bh = blockIdx.y;
@@ -151,13 +171,25 @@ __global__ void __launch_bounds__(THREADS, 1)
         tma_load_4d(&map_q, q_full, smem + Smem::Q, 0, q0, h, b);
         tma_load_4d(&map_q, q_full, smem + Smem::Q + TILE_BYTES, 0, q0 + BM, h, b);
       }
+      // constant A_x tile and zeroed B_x tiles (only columns 0-1 change later)
+      {
+        uint32_t* w = reinterpret_cast<uint32_t*>(smem + Smem::ONES);
+        for (int i = lane; i < (XTILE_BYTES * (1 + STAGES)) / 4; i += 32) w[i] = 0u;
+        __syncwarp();
+        for (int row = lane; row < BM; row += 32)
+          *reinterpret_cast<uint32_t*>(smem + Smem::ONES + xtile_off(row, 0)) = 0x3F803F80u;  // 1, 1
+      }
       // bias of the next tile is fetched into registers one tile ahead
-      float bnext[BN / 32];
+      const float inv_scale = 1.0f / p.scale;
+      uint32_t bnext[BN / 32];
       auto fetch_bias = [&](int j) {
 #pragma unroll
         for (int i = 0; i < BN / 32; ++i) {
           const int col = j * BN + i * 32 + lane;
-          bnext[i] = col < p.n ? (brow ? __ldg(brow + col) * 1.4426950408889634f : 0.0f) : -INFINITY;
+          const float beta = col < p.n ? (brow ? __ldg(brow + col) * inv_scale : 0.0f) : kMaskedBeta;
+          const __nv_bfloat16 hi = __float2bfloat16_rn(beta);
+          const __nv_bfloat16 lo = __float2bfloat16_rn(beta - __bfloat162float(hi));
+          bnext[i] = (uint32_t)__bfloat16_as_ushort(hi) | ((uint32_t)__bfloat16_as_ushort(lo) << 16);
         }
       };
       fetch_bias(0);
@@ -166,9 +198,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t ph = (j / STAGES) & 1;
         bool okw = wait_bar(&kv_empty[s], ph ^ 1, abort_flag, p.status, kDevTimeout);
         if (!__all_sync(0xffffffffu, okw)) break;
-        float* bt = sbias + s * BN;
+        uint8_t* bt = smem + Smem::BIAS + s * XTILE_BYTES;
 #pragma unroll
-        for (int i = 0; i < BN / 32; ++i) bt[i * 32 + lane] = bnext[i];
+        for (int i = 0; i < BN / 32; ++i)
+          *reinterpret_cast<uint32_t*>(bt + xtile_off(i * 32 + lane, 0)) = bnext[i];
+        fence_async_smem();   // generic-proxy writes -> tensor core reads
         __syncwarp();
         if (lane == 0) {
           bar_expect_tx(&kv_full[s], 2 * TILE_BYTES);
@@ -192,6 +226,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t sQ = smem_u32(smem + Smem::Q);
         const uint32_t sK = smem_u32(smem + Smem::K);
         const uint32_t sV = smem_u32(smem + Smem::V);
+        const uint32_t sOnes = smem_u32(smem + Smem::ONES);
+        const uint32_t sBias = smem_u32(smem + Smem::BIAS);
         auto issue_s = [&](int t, int j) {
           const uint32_t kaddr = sK + (j % STAGES) * TILE_BYTES;
           const uint32_t qaddr = sQ + t * TILE_BYTES;
@@ -199,6 +235,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int k = 0; k < HD / 16; ++k)
             umma_bf16(tbase + t * BN, sdesc_sw128(qaddr + k * 32, 16, 1024),
                       sdesc_sw128(kaddr + k * 32, 16, 1024), idesc_s, k != 0);
+          umma_bf16(tbase + t * BN, sdesc_none(sOnes), sdesc_none(sBias + (j % STAGES) * XTILE_BYTES),
+                    idesc_s, 1);  // + beta_j
           umma_commit(&s_full[t]);
         };
         auto issue_o = [&](int t, int j) {
@@ -271,7 +309,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t tS = tbase + lane_off + t * BN;
     const uint32_t tO = tbase + lane_off + 256 + t * HD;
     const uint32_t tP = tbase + lane_off + 384 + t * 64;
-    float m_ref = -INFINITY, l = 0.f;
+    float m_raw = -INFINITY, l = 0.f;   // running max of S' (raw units), row sum
     bool okw = true;
     for (int j = 0; j < nk; ++j) {
       const int s = j % STAGES;
@@ -287,56 +325,38 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) bar_arrive(&s_empty[t]);
 
-      const float4* bt = reinterpret_cast<const float4*>(sbias + s * BN);
+      // x holds S' = q.k + beta (raw units); max on the raw scores
       float mx[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) mx[i] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < BN / 4; ++c) {
-        const float4 bb = bt[c];
-        ffma2(x[4 * c + 0], x[4 * c + 1], x[4 * c + 0], x[4 * c + 1], p.scale_log2, p.scale_log2,
-              bb.x, bb.y);
-        ffma2(x[4 * c + 2], x[4 * c + 3], x[4 * c + 2], x[4 * c + 3], p.scale_log2, p.scale_log2,
-              bb.z, bb.w);
         mx[c & 3] = fmax3(mx[c & 3], x[4 * c + 0], x[4 * c + 1]);
         mx[c & 3] = fmax3(mx[c & 3], x[4 * c + 2], x[4 * c + 3]);
       }
       const float mt = fmax3(fmaxf(mx[0], mx[1]), mx[2], mx[3]);
       float alpha = 1.f;
-      const bool moved = mt > m_ref + kRescaleThreshold;
+      const bool moved = (mt - m_raw) * p.scale_log2 > kRescaleThreshold;  // also when m_raw = -inf
       if (moved) {
-        alpha = fast_exp2(m_ref - mt);  // 0 on the first tile (m_ref = -inf)
+        alpha = fast_exp2((m_raw - mt) * p.scale_log2);  // 0 on the first tile
         l *= alpha;
-        m_ref = mt;
+        m_raw = mt;
       }
       float acc[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-      const float neg_m = -m_ref;
-#if GPA_ATTN_EXP_FIRST
-      // all exponentials first (independent streams for the scheduler), in place
-#pragma unroll
-      for (int g = 0; g < 16; ++g) {
-        float* xg = x + g * 8;
-#pragma unroll
-        for (int i = 0; i < 8; i += 2) fadd2(xg[i], xg[i + 1], xg[i], xg[i + 1], neg_m, neg_m);
-        exp8(xg, xg);
-      }
-#endif
+      const float neg_mc = -m_raw * p.scale_log2;
+      const float c2 = p.scale_log2;
 #pragma unroll
       for (int qt = 0; qt < 4; ++qt) {  // 32 keys -> 16 packed bf16 pairs per quarter
         uint32_t pk[16];
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
           float* xg = x + qt * 32 + g * 8;
-#if GPA_ATTN_EXP_FIRST
-          const float* e = xg;
-#else
 #pragma unroll
-          for (int i = 0; i < 8; i += 2) fadd2(xg[i], xg[i + 1], xg[i], xg[i + 1], neg_m, neg_m);
+          for (int i = 0; i < 8; i += 2) ffma2(xg[i], xg[i + 1], xg[i], xg[i + 1], c2, c2, neg_mc, neg_mc);
           float e[8];
           exp8(xg, e);
-#endif
 #pragma unroll
           for (int i = 0; i < 8; i += 2) fadd2(acc[i], acc[i + 1], acc[i], acc[i + 1], e[i], e[i + 1]);
 #pragma unroll
@@ -394,7 +414,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           pk.w = pack_bf16x2(__uint_as_float(ov[8 * u + 6]) * inv, __uint_as_float(ov[8 * u + 7]) * inv);
           reinterpret_cast<uint4*>(orow)[u] = pk;
         }
-        if (p.lse) p.lse[(int64_t)b * p.lse_sb + (int64_t)h * p.lse_sh + row] = m_ref + __log2f(l);
+        if (p.lse)
+          p.lse[(int64_t)b * p.lse_sb + (int64_t)h * p.lse_sh + row] = m_raw * p.scale_log2 + __log2f(l);
       }
     }
   }
@@ -471,6 +492,7 @@ extern "C" int gpa_attention_keybias(const void* q, const void* k, const void* v
   if (rc) return rc;
   Params p;
   p.m = m; p.n = n; p.heads = heads;
+  p.scale = sm_scale;
   p.scale_log2 = sm_scale * 1.4426950408889634f;
   p.bias = bias; p.bias_sb = bias_sb; p.bias_sh = bias_sh;
   p.o = (__nv_bfloat16*)o; p.o_sb = o_sb; p.o_sh = o_sh; p.o_sm = o_sm;

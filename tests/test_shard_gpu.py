@@ -1,0 +1,65 @@
+"""Query-frame sharding on real GPUs (NCCL): the S-frame GPA forward split over
+two ranks against the same forward on one GPU.  Merge decisions near a tie can
+flip when a GEMM tiles differently for fewer rows, so the bound is bf16-level:
+rel-L2 < 1e-2 on the last aggregator tap, the depth and the camera encoding."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")]
+
+S = 4
+
+
+def _rel(a, b):
+    return float((a.double() - b.double()).norm() / b.double().norm())
+
+
+def _worker(rank, world, port, outdir):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    import datetime
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=300),
+                            device_id=torch.device("cuda", rank))
+    from bench import build_model, forward
+    from gpa_vggt_b200.vggt.shard import FrameShard
+    dev = torch.device("cuda", rank)
+    model = build_model(dev)
+    images = torch.rand(1, S, 3, 518, 518, generator=torch.Generator().manual_seed(0)).to(torch.bfloat16)
+    shard = FrameShard(S)
+    model.set_shard(shard)
+    pose, depth, conf = forward(model, images[:, shard.f0:shard.f1].contiguous().to(dev))
+    torch.save({"pose": pose.float().cpu(), "depth": depth.float().cpu(), "f0": shard.f0,
+                "f1": shard.f1}, os.path.join(outdir, f"r{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_sharded_forward_matches_single_gpu(tmp_path):
+    world = 2
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       start_method="spawn")
+    from bench import build_model, forward
+    model = build_model(torch.device("cuda", 0))
+    images = torch.rand(1, S, 3, 518, 518, generator=torch.Generator().manual_seed(0)).to(torch.bfloat16)
+    pose, depth, conf = forward(model, images.cuda())
+    for r in range(world):
+        got = torch.load(tmp_path / f"r{r}.pt")
+        e_pose = _rel(got["pose"], pose.float().cpu())
+        e_depth = _rel(got["depth"], depth[:, got["f0"]:got["f1"]].float().cpu())
+        print(f"rank {r}: rel-L2 pose {e_pose:.2e} depth {e_depth:.2e}")
+        assert e_pose < 1e-2 and e_depth < 1e-2
