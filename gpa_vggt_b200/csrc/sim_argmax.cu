@@ -160,19 +160,29 @@ __global__ void __launch_bounds__(Cfg<KC>::THREADS, 1)
       if (lane == 0) bar_arrive(&acc_empty[buf]);
       const int col0 = j * BN;
       const int valid = min(BN, n - col0);
+      if (valid < BN) {  // last tile: mask the columns past n
+#pragma unroll
+        for (int i = 0; i < BN; ++i)
+          if (i >= valid) r[i] = __float_as_uint(-INFINITY);
+      }
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
-        float cmax = -INFINITY;
+        const uint32_t* rc = r + c * 32;
+        // tree of 3-input maxima (short dependency chains)
+        float m1[11];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float v = (c * 32 + i < valid) ? __uint_as_float(r[c * 32 + i]) : -INFINITY;
-          cmax = fmaxf(cmax, v);
-        }
+        for (int i = 0; i < 10; ++i)
+          m1[i] = fmax3(__uint_as_float(rc[3 * i]), __uint_as_float(rc[3 * i + 1]),
+                        __uint_as_float(rc[3 * i + 2]));
+        m1[10] = fmaxf(__uint_as_float(rc[30]), __uint_as_float(rc[31]));
+        const float m2a = fmax3(m1[0], m1[1], m1[2]), m2b = fmax3(m1[3], m1[4], m1[5]);
+        const float m2c = fmax3(m1[6], m1[7], m1[8]), m2d = fmaxf(m1[9], m1[10]);
+        const float cmax = fmaxf(fmaxf(m2a, m2b), fmaxf(m2c, m2d));
         if (cmax > best) {  // strict: an equal later score keeps the earlier index
           int first = 0;
 #pragma unroll
           for (int i = 31; i >= 0; --i)
-            if (c * 32 + i < valid && __uint_as_float(r[c * 32 + i]) == cmax) first = i;
+            if (__uint_as_float(rc[i]) == cmax) first = i;
           best = cmax;
           bidx = col0 + c * 32 + first;
         }
