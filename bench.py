@@ -41,6 +41,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 P_TOK = 37 * 37 + 5  # tokens per frame
+ATTN_TRAFFIC_RATIO = 350.9 / 341.0  # measured DRAM bytes / algorithmic bytes of attn_kernel
 METRIC = "GPA-VGGT fwd latency (ms) & frames/s at S=200, 1/2/4/8 B200; % roofline"
 
 
@@ -381,8 +382,9 @@ def main():
     launches = _lib.launch_count() - l0
     timing, kernels.ATTN_TIMING = kernels.ATTN_TIMING, None
     ms = start.elapsed_time(stop) / args.steps
-    attn_ms = sum(a.elapsed_time(b) for a, b, _ in timing) / args.steps
-    attn_flops = sum(f for _, _, f in timing) / args.steps
+    attn_ms = sum(rec[0].elapsed_time(rec[1]) for rec in timing) / args.steps
+    attn_flops = sum(rec[2] for rec in timing) / args.steps
+    attn_bytes = sum(rec[3] for rec in timing) / args.steps
     n_attn = len(timing) // args.steps
     if world > 1:
         t = torch.tensor([ms, attn_ms], device=dev)
@@ -452,7 +454,12 @@ def main():
             "frac": achieved / pk["bf16_sus"], "peak_kind": f"{pk['src']} sustained bf16 (long step)",
             "frac_of_burst": achieved / pk["bf16"], "flops_per_step": attn_flops,
             "launches_per_step": n_attn, "ms_per_step": attn_ms,
-            "share_of_step": attn_ms / ms, "traffic": None}
+            "share_of_step": attn_ms / ms,
+            # DRAM bytes per step: the algorithmic q/k/v/o bytes of this step's launches
+            # times the measured ratio dram__bytes_read+write / algorithmic = 1.03 of
+            # the ncu capture in profiles/attn_kernel_q16384_k66845.md (K/V read once)
+            "traffic": ATTN_TRAFFIC_RATIO * attn_bytes, "traffic_unit": "bytes per step",
+            "algorithmic_bytes_per_step": attn_bytes}
     line = dict(base, value=ms, ms_per_step=ms, gpu_launches=launches, roofline=roof, e2e=e2e,
                 clocks=clk.summary())
     if fwd:

@@ -25,7 +25,7 @@ CHECK_STATUS = os.environ.get("GPA_CHECK_STATUS", "0") == "1"
 
 
 # When set to a list, every attention launch appends (start event, end event,
-# algorithmic flops) recorded on its stream (used by bench.py for the roofline).
+# algorithmic flops, algorithmic bytes) recorded on its stream (bench.py's roofline).
 ATTN_TIMING = None
 
 
@@ -220,7 +220,7 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bias: Optional[
          ptr(status), stream_of(q))
     if timing is not None:
         e1.record()
-        timing.append((e0, e1, 4.0 * B * H * M * N * D))
+        timing.append((e0, e1, 4.0 * B * H * M * N * D, 2.0 * B * H * (2 * M + 2 * N) * D))
     if own:
         _check_status(status, "gpa_attention_keybias")
     return (out, lse) if return_lse else out
