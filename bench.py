@@ -465,7 +465,7 @@ def main():
     if fwd:
         line["frames_per_s"] = S / (ms / 1e3)
         line["gpu_memory_peak_gib"] = torch.cuda.max_memory_allocated(dev) / 2 ** 30
-    if rank == 0 and not args.no_cpu:
+    if world == 1 and not args.no_cpu:   # the CPU baseline is an N=1 figure
         if fwd:
             cms, sample = cpu_forward_ms(S, args.vanilla)
         else:

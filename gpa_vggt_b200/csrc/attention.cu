@@ -7,26 +7,30 @@
 //
 // B200 design (one CTA = two 128-query tiles of one (batch, head); 384 threads):
 //   warp 0      TMA producer: Q tiles once, then K/V tiles through a 3-stage
-//               ring; stages each tile's bias row (x log2 e, -inf past n).
-//   warp 1      one thread issues tcgen05.mma: S_t = Q_t K^T (A and B from
-//               shared memory) and O_t += P_t V (P_t from TMEM, V from shared
-//               memory), ping-ponging the two query tiles so the tensor core
-//               works on one tile while the other is in softmax.
+//               ring; writes each key tile's bias/scale as a bf16 hi/lo pair
+//               (-1e30 past n) for the extra K step of the score MMA.
+//   warps 1, 2  MMA issuers, one per query tile t: S_t = Q_t K^T + beta (A
+//               and B from shared memory) and O_t += P_t V (P_t from TMEM, V
+//               from shared memory); the tensor core takes work from whichever
+//               issuer is ready, so one tile's MMAs run while the other tile
+//               is in softmax.
 //   warps 4-11  two softmax warpgroups, one per query tile, thread == row:
 //               S from TMEM -> online softmax -> P (bf16) back into TMEM.
 //               The running max only moves when it grows by more than 2^8
-//               (lazy rescale of O in TMEM); 3/8 of the exponentials run as a
+//               (lazy rescale of O in TMEM); 2/8 of the exponentials run as a
 //               polynomial on the FMA pipe to offload the MUFU unit (16/clk/SM);
 //               scale/bias, max and sum use packed fp32x2 and 3-input max with
 //               independent accumulators.
-//   MMA order:  out of order across the two tiles: S_t(j+1) is issued as soon
-//               as softmax t has pulled S_t(j) into registers, O_t += P_t(j) V_j
-//               as soon as P_t(j) is in TMEM, whichever comes first, so neither
-//               softmax warpgroup waits on the other's progress.
+//   MMA order:  per tile, S_t(j+1) as soon as softmax t has pulled S_t(j)
+//               into registers, O_t += P_t(j) V_j as soon as P_t(j) is in TMEM;
+//               the two tiles' issuers are independent warps, so neither
+//               waits on the other's progress (a single polling issuer spent
+//               most of its time in shared-memory barrier probes, which are
+//               slow while the MMAs stream their operands).
 //   TMEM (512 columns): S0 0..127, S1 128..255, O0 256..319, O1 320..383,
 //                       P0 384..447, P1 448..511 (P: two bf16 per column).
 //   The producer/MMA warpgroup gives registers to the softmax warpgroups
-//   (setmaxnreg 56 / 216).
+//   (setmaxnreg 80 / 208: the split that leaves both sides without spills).
 #include "common.cuh"
 #include "capi_util.h"
 
@@ -36,13 +40,16 @@ namespace attn {
 constexpr int BM = 128;   // queries per tile
 constexpr int BN = 128;   // keys per tile
 constexpr int HD = 64;    // head dim
-constexpr int STAGES = 3;
+#ifndef GPA_ATTN_STAGES
+#define GPA_ATTN_STAGES 3
+#endif
+constexpr int STAGES = GPA_ATTN_STAGES;   // K/V ring depth
 constexpr int TILE_BYTES = BM * HD * 2;  // 16 KB
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 constexpr int THREADS = 384;
 constexpr int TMEM_COLS = 512;
 #ifndef GPA_ATTN_REGS_LOW
-#define GPA_ATTN_REGS_LOW 56
+#define GPA_ATTN_REGS_LOW 80
 #endif
 constexpr int REGS_LOW = GPA_ATTN_REGS_LOW, REGS_HIGH = (168 * 384 - GPA_ATTN_REGS_LOW * 128) / 256 / 8 * 8,
               REGS_LAUNCH = 168;
@@ -70,6 +77,8 @@ struct Smem {
   static constexpr int TOTAL = BARS + 256;
   static constexpr int ALLOC = TOTAL + 1024;
 };
+static_assert(Smem::ALLOC <= 232448, "shared memory per CTA");
+static_assert((9 + 2 * STAGES) * 8 + 8 <= 256, "barrier area");
 
 struct Params {
   int m, n, heads;
@@ -85,11 +94,17 @@ struct Params {
 };
 
 // How many of each group of 8 exponentials run as the FMA-pipe polynomial
-// (the rest on MUFU, 16/clk/SM); 3 balances MUFU against issue slots.
+// (the rest on MUFU, 16/clk/SM); 2 was fastest in a sweep of 1-4.
 #ifndef GPA_ATTN_POLY_PER8
-#define GPA_ATTN_POLY_PER8 3
+#define GPA_ATTN_POLY_PER8 2
 #endif
 constexpr int kPolyPer8 = GPA_ATTN_POLY_PER8;
+// Quarter of a key tile's exponentials after which softmax waits for the
+// previous O_t += P_t V (P_t and O_t in TMEM are busy until then).
+#ifndef GPA_ATTN_ODONE_Q
+#define GPA_ATTN_ODONE_Q 1
+#endif
+constexpr int kOdoneQuarter = GPA_ATTN_ODONE_Q;
 
 
 // no-swizzle K-major descriptor of an extra-step tile
@@ -137,7 +152,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     bar_init(q_full, 1);
     for (int s = 0; s < STAGES; ++s) {
       bar_init(&kv_full[s], 1);
-      bar_init(&kv_empty[s], 1);
+      bar_init(&kv_empty[s], 2);   // one arrival per query tile's issuer
     }
     for (int t = 0; t < 2; ++t) {
       bar_init(&s_full[t], 1);
@@ -186,7 +201,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int i = 0; i < BN / 32; ++i) {
           const int col = j * BN + i * 32 + lane;
-          const float beta = col < p.n ? (brow ? __ldg(brow + col) * inv_scale : 0.0f) : kMaskedBeta;
+          // -inf (or NaN) bias behaves like a key past n
+          const float beta = col < p.n ? fmaxf(brow ? __ldg(brow + col) * inv_scale : 0.0f, kMaskedBeta)
+                                       : kMaskedBeta;
           const __nv_bfloat16 hi = __float2bfloat16_rn(beta);
           const __nv_bfloat16 lo = __float2bfloat16_rn(beta - __bfloat162float(hi));
           bnext[i] = (uint32_t)__bfloat16_as_ushort(hi) | ((uint32_t)__bfloat16_as_ushort(lo) << 16);
@@ -218,85 +235,70 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int j = max(0, issued - STAGES); j < issued; ++j)
           drain_bar(&kv_full[j % STAGES], (j / STAGES) & 1, t0);
       }
-    } else if (warp == 1) {
-      // ------------------------------ MMA issuer ------------------------------
-      if (elect_one()) {
-        constexpr uint32_t idesc_s = idesc_bf16(BM, BN, false, false);
-        constexpr uint32_t idesc_o = idesc_bf16(BM, HD, false, true);
-        const uint32_t sQ = smem_u32(smem + Smem::Q);
-        const uint32_t sK = smem_u32(smem + Smem::K);
-        const uint32_t sV = smem_u32(smem + Smem::V);
-        const uint32_t sOnes = smem_u32(smem + Smem::ONES);
-        const uint32_t sBias = smem_u32(smem + Smem::BIAS);
-        auto issue_s = [&](int t, int j) {
-          const uint32_t kaddr = sK + (j % STAGES) * TILE_BYTES;
-          const uint32_t qaddr = sQ + t * TILE_BYTES;
+    } else if (warp == 1 || warp == 2) {
+      // ------------------------------ MMA issuers ------------------------------
+      // One issuer warp per query tile t (warp 1 -> tile 0, warp 2 -> tile 1),
+      // each in order: S_t(j+1) once softmax t holds S_t(j) and K_{j+1} has
+      // landed, then O_t += P_t(j) V_j once P_t(j) is in TMEM.  While one
+      // issuer waits on its barriers, the other keeps the tensor core fed.
+      // Each releases a K/V stage after its PV of that key tile (the empty
+      // barrier counts both).  The warp runs the loop converged so descriptor
+      // math stays warp-uniform; one elected lane issues and commits.
+      // Moving a descriptor by b bytes within shared memory adds b/16 to it.
+      const int t = warp - 1;
+      const bool leader = elect_one();
+      constexpr uint32_t idesc_s = idesc_bf16(BM, BN, false, false);
+      constexpr uint32_t idesc_o = idesc_bf16(BM, HD, false, true);
+      const uint64_t dQ = sdesc_sw128(smem_u32(smem + Smem::Q + t * TILE_BYTES), 16, 1024);
+      const uint64_t dK = sdesc_sw128(smem_u32(smem + Smem::K), 16, 1024);
+      const uint64_t dV = sdesc_sw128(smem_u32(smem + Smem::V), 16384, 1024);
+      const uint64_t dOnes = sdesc_none(smem_u32(smem + Smem::ONES));
+      const uint64_t dBias = sdesc_none(smem_u32(smem + Smem::BIAS));
+      const uint32_t dS = tbase + t * BN, dO = tbase + 256 + t * HD, tPm = tbase + 384 + t * 64;
+      auto issue_s = [&](int j) {
+        const int st = j % STAGES;
+        const uint64_t bk = dK + (uint64_t)(st * (TILE_BYTES >> 4));
+        const uint64_t bb = dBias + (uint64_t)(st * (XTILE_BYTES >> 4));
+        if (leader) {
 #pragma unroll
-          for (int k = 0; k < HD / 16; ++k)
-            umma_bf16(tbase + t * BN, sdesc_sw128(qaddr + k * 32, 16, 1024),
-                      sdesc_sw128(kaddr + k * 32, 16, 1024), idesc_s, k != 0);
-          umma_bf16(tbase + t * BN, sdesc_none(sOnes), sdesc_none(sBias + (j % STAGES) * XTILE_BYTES),
-                    idesc_s, 1);  // + beta_j
+          for (int k = 0; k < HD / 16; ++k) umma_bf16(dS, dQ + 2 * k, bk + 2 * k, idesc_s, k != 0);
+          umma_bf16(dS, dOnes, bb, idesc_s, 1);  // + beta_j
           umma_commit(&s_full[t]);
-        };
-        auto issue_o = [&](int t, int j) {
-          const uint32_t vaddr = sV + (j % STAGES) * TILE_BYTES;
-          const uint32_t ptm = tbase + 384 + t * 64;
+        }
+        __syncwarp();
+      };
+      auto issue_o = [&](int j) {
+        const uint64_t bv = dV + (uint64_t)((j % STAGES) * (TILE_BYTES >> 4));
+        if (leader) {
 #pragma unroll
           for (int ks = 0; ks < BN / 16; ++ks)
-            umma_bf16_ts(tbase + 256 + t * HD, ptm + ks * 8, sdesc_sw128(vaddr + ks * 2048, 16384, 1024),
-                         idesc_o, (j > 0 || ks > 0));
+            umma_bf16_ts(dO, tPm + ks * 8, bv + (uint64_t)(ks * (2048 >> 4)), idesc_o, (j > 0 || ks > 0));
           umma_commit(&o_done[t]);
-        };
-        bool okw = wait_bar(q_full, 0, abort_flag, p.status, kDevTimeout) &&
-                   wait_bar(&kv_full[0], 0, abort_flag, p.status, kDevTimeout);
-        if (okw) {
+          umma_commit(&kv_empty[j % STAGES]);
+        }
+        __syncwarp();
+      };
+      bool okw = wait_bar(q_full, 0, abort_flag, p.status, kDevTimeout) &&
+                 wait_bar(&kv_full[0], 0, abort_flag, p.status, kDevTimeout);
+      okw = __all_sync(0xffffffffu, okw);
+      if (okw) {
+        tc_fence_after();
+        issue_s(0);
+      }
+      for (int j = 0; okw && j < nk; ++j) {
+        if (j + 1 < nk) {
+          okw = wait_bar(&s_empty[t], j & 1, abort_flag, p.status, kDevTimeout) &&
+                wait_bar(&kv_full[(j + 1) % STAGES], ((j + 1) / STAGES) & 1, abort_flag, p.status,
+                         kDevTimeout);
+          okw = __all_sync(0xffffffffu, okw);
+          if (!okw) break;
           tc_fence_after();
-          issue_s(0, 0);
-          issue_s(1, 0);
+          issue_s(j + 1);
         }
-        // Issue whatever is ready, per query tile t: S_t(j) once softmax t holds
-        // S_t(j-1) and K_j has landed; O_t += P_t(j) V_j once P_t(j) is written.
-        // A K/V stage is released after both tiles' PV of that key tile.
-        int s_next[2] = {1, 1}, pv_next[2] = {0, 0}, released = 0;
-        unsigned long long idle_since = 0;
-        while (okw && (pv_next[0] < nk || pv_next[1] < nk)) {
-          bool progressed = false;
-#pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const int js = s_next[t];
-            if (js < nk && bar_try_wait(&s_empty[t], (js - 1) & 1) &&
-                bar_try_wait(&kv_full[js % STAGES], (js / STAGES) & 1)) {
-              tc_fence_after();
-              issue_s(t, js);
-              s_next[t] = js + 1;
-              progressed = true;
-            }
-            const int jp = pv_next[t];
-            if (jp < nk && bar_try_wait(&p_full[t], jp & 1)) {
-              tc_fence_after();
-              issue_o(t, jp);
-              pv_next[t] = jp + 1;
-              progressed = true;
-            }
-          }
-          const int both = min(pv_next[0], pv_next[1]);
-          while (released < both) {
-            umma_commit(&kv_empty[released % STAGES]);
-            ++released;
-          }
-          if (progressed) {
-            idle_since = 0;
-          } else if (idle_since == 0) {
-            idle_since = global_ns();
-          } else if (*abort_flag) {
-            okw = false;
-          } else if (global_ns() - idle_since > kWaitLimitNs) {
-            *abort_flag = 1;
-            if (p.status) atomicExch(p.status, kDevTimeout);
-            okw = false;
-          }
-        }
+        okw = __all_sync(0xffffffffu, wait_bar(&p_full[t], j & 1, abort_flag, p.status, kDevTimeout));
+        if (!okw) break;
+        tc_fence_after();
+        issue_o(j);
       }
     }
   } else {
@@ -310,13 +312,40 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t tO = tbase + lane_off + 256 + t * HD;
     const uint32_t tP = tbase + lane_off + 384 + t * 64;
     float m_raw = -INFINITY, l = 0.f;   // running max of S' (raw units), row sum
+    const float c2 = p.scale_log2;
     bool okw = true;
+    // 32 keys of one row: y = c*(x - m) (packed FMA, in place), P = 2^y (MUFU /
+    // polynomial), row-sum accumulators, bf16 pairs
+    auto quarter = [&](float* xq, float neg_mc, float* acc, uint32_t* pk) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        float* xg = xq + g * 8;
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) ffma2(xg[i], xg[i + 1], xg[i], xg[i + 1], c2, c2, neg_mc, neg_mc);
+        float e[8];
+        exp8(xg, e);
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) fadd2(acc[i], acc[i + 1], acc[i], acc[i + 1], e[i], e[i + 1]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pk[g * 4 + i] = pack_bf16x2(e[2 * i], e[2 * i + 1]);
+      }
+    };
+    auto rescale_o = [&](float alpha) {
+      uint32_t ov[32];
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        tmem_ld32(tO + hf * 32, ov);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+        tmem_st32(tO + hf * 32, ov);
+      }
+    };
     for (int j = 0; j < nk; ++j) {
-      const int s = j % STAGES;
-      okw = wait_bar(&s_full[t], j & 1, abort_flag, p.status, kDevTimeout) &&
-            wait_bar(&kv_full[s], (j / STAGES) & 1, abort_flag, p.status, kDevTimeout);
+      okw = wait_bar(&s_full[t], j & 1, abort_flag, p.status, kDevTimeout);
       if (!__all_sync(0xffffffffu, okw)) { okw = false; break; }
       tc_fence_after();
+      // x holds S' = q.k + beta (raw units); max on the raw scores
       float x[BN];
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) tmem_ld32f(tS + c * 32, x + c * 32);
@@ -324,11 +353,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) bar_arrive(&s_empty[t]);
-
-      // x holds S' = q.k + beta (raw units); max on the raw scores
-      float mx[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) mx[i] = -INFINITY;
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < BN / 4; ++c) {
         mx[c & 3] = fmax3(mx[c & 3], x[4 * c + 0], x[4 * c + 1]);
@@ -336,55 +361,36 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       const float mt = fmax3(fmaxf(mx[0], mx[1]), mx[2], mx[3]);
       float alpha = 1.f;
-      const bool moved = (mt - m_raw) * p.scale_log2 > kRescaleThreshold;  // also when m_raw = -inf
+      const bool moved = (mt - m_raw) * c2 > kRescaleThreshold;  // also when m_raw = -inf
       if (moved) {
-        alpha = fast_exp2((m_raw - mt) * p.scale_log2);  // 0 on the first tile
+        alpha = fast_exp2((m_raw - mt) * c2);  // 0 on the first tile
         l *= alpha;
         m_raw = mt;
       }
-      float acc[8];
+      const float neg_mc = -m_raw * c2;
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[4][16];   // packed bf16 pairs, 32 keys per quarter
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-      const float neg_mc = -m_raw * p.scale_log2;
-      const float c2 = p.scale_log2;
-#pragma unroll
-      for (int qt = 0; qt < 4; ++qt) {  // 32 keys -> 16 packed bf16 pairs per quarter
-        uint32_t pk[16];
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          float* xg = x + qt * 32 + g * 8;
-#pragma unroll
-          for (int i = 0; i < 8; i += 2) ffma2(xg[i], xg[i + 1], xg[i], xg[i + 1], c2, c2, neg_mc, neg_mc);
-          float e[8];
-          exp8(xg, e);
-#pragma unroll
-          for (int i = 0; i < 8; i += 2) fadd2(acc[i], acc[i + 1], acc[i], acc[i + 1], e[i], e[i + 1]);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) pk[g * 4 + i] = pack_bf16x2(e[2 * i], e[2 * i + 1]);
-        }
+      for (int qt = 0; qt < 4; ++qt) {
+        quarter(x + qt * 32, neg_mc, acc, pk[qt]);
         // P_t and O_t are free once the previous O_t += P_t V finished; the
-        // first quarter of the exponentials hides that wait
-        if (qt == 0 && j > 0) {
-          okw = wait_bar(&o_done[t], (j - 1) & 1, abort_flag, p.status, kDevTimeout);
-          if (!__all_sync(0xffffffffu, okw)) { okw = false; break; }
-          tc_fence_after();
+        // first kOdoneQuarter+1 quarters of the exponentials hide that wait
+        if (qt == kOdoneQuarter) {
+          if (j > 0) {
+            okw = wait_bar(&o_done[t], (j - 1) & 1, abort_flag, p.status, kDevTimeout);
+            if (!__all_sync(0xffffffffu, okw)) { okw = false; break; }
+            tc_fence_after();
+          }
+#pragma unroll
+          for (int u = 0; u <= kOdoneQuarter; ++u) tmem_st16(tP + u * 16, pk[u]);
+        } else if (qt > kOdoneQuarter) {
+          tmem_st16(tP + qt * 16, pk[qt]);
         }
-        tmem_st16(tP + qt * 16, pk);
       }
       if (!okw) break;
       l += ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
       // rescale O_t in TMEM where the running max moved
-      if (j > 0 && __any_sync(0xffffffffu, moved)) {
-        uint32_t ov[32];
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          tmem_ld32(tO + hf * 32, ov);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-          tmem_st32(tO + hf * 32, ov);
-        }
-      }
+      if (j > 0 && __any_sync(0xffffffffu, moved)) rescale_o(alpha);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();

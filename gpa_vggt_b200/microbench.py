@@ -33,16 +33,45 @@ def peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+LAST_CLOCKS: dict = {}
+
+
+def _sm_clock_sampler(stop, out):
+    """Median SM clock (MHz) of the current GPU while `stop` is unset (NVML)."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByIndex(torch.cuda.current_device())
+        vals = []
+        while not stop.is_set():
+            vals.append(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+            stop.wait(0.005)
+        if vals:
+            vals.sort()
+            out["sm_mhz"] = vals[len(vals) // 2]
+            out["samples"] = len(vals)
+    except Exception as e:  # no NVML: report the reason, timing is unaffected
+        out["error"] = str(e)[:80]
+
+
 def timed(fn, iters, warmup):
+    import threading
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
+    stop, clk = threading.Event(), {}
+    th = threading.Thread(target=_sm_clock_sampler, args=(stop, clk), daemon=True)
+    th.start()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(iters):
         fn()
     b.record()
     torch.cuda.synchronize()
+    stop.set()
+    th.join()
+    LAST_CLOCKS.clear()
+    LAST_CLOCKS.update(clk)
     return a.elapsed_time(b) / iters
 
 
@@ -68,7 +97,7 @@ def bench_attn(lq, lk, heads=16, bias=True, iters=5, warmup=2, seed=0):
     tf = flops / ms / 1e9
     return {"kernel": "attention", "lq": lq, "lk": lk, "heads": heads, "bias": bias, "ms": ms,
             "tflops": tf, "peak_tflops": peak, "frac": tf / peak, "peak_src": src,
-            "status": int(status.item())}
+            "status": int(status.item()), "clocks": dict(LAST_CLOCKS)}
 
 
 def bench_sim(m, n, d=128, iters=5, warmup=2, seed=0):

@@ -214,6 +214,30 @@ def test_attention_strided_views_and_large_logits():
     assert rel_l2(o, ref) < 1e-2
 
 
+@pytest.mark.parametrize("ramp", [2.0, 40.0, 120.0])
+def test_attention_running_max_moves_along_keys(ramp):
+    """A bias that rises along the keys moves the row max on many key tiles
+    (ramp 120: about 15 log2 units per 128-key tile, past the lazy-rescale
+    threshold every tile); in head 1 the first 200 keys have -inf bias, so
+    the max jumps from the masked value on the second tile.  Tiles whose
+    exponentials were taken against a stale max must be redone, and O
+    rescaled, without changing the result."""
+    from gpa_vggt_b200 import kernels
+    g = torch.Generator().manual_seed(int(ramp))
+    B, H, M, N = 1, 2, 300, 1500
+    q = torch.randn(B, H, M, 64, generator=g).bfloat16()
+    k = torch.randn(B, H, N, 64, generator=g).bfloat16()
+    v = torch.randn(B, H, N, 64, generator=g).bfloat16()
+    bias = torch.linspace(0.0, ramp, N).expand(B, H, N).clone()
+    bias[:, 1, :200] = float("-inf")
+    scale = 64 ** -0.5
+    o, lse = kernels.attention(q.to(DEV), k.to(DEV), v.to(DEV), bias.to(DEV), scale, return_lse=True)
+    ro, rlse = O.attention_keybias(q, k, v, bias[:, :, None, :], scale, return_lse=True)
+    assert torch.isfinite(o.float()).all()
+    assert rel_l2(o, ro) < 1e-2
+    assert float((lse.cpu().double() - rlse).abs().max()) < 2e-3
+
+
 def test_attention_matches_reference_golden(golden):
     """Against the reference Triton kernel's own output (interpreter run)."""
     from gpa_vggt_b200.merging.fused_attention import attention_keybias
