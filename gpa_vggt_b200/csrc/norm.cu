@@ -6,6 +6,8 @@
 //    2D rotary embedding (vggt/layers/attention.py:216-220, rope.py:139-209),
 //    in fp32 registers, written back as bf16 -- one pass over the qkv buffer
 //    instead of the norm, rotate, concatenate and cast kernels.
+//  * gpa_residual_scale_bf16: the residual add of a LayerScale branch,
+//    x + y * gamma, in one pass (vggt/layers/block.py:88,94).
 #include "common.cuh"
 #include "capi_util.h"
 
@@ -159,6 +161,41 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
 }  // namespace norm
 }  // namespace gpa
 
+namespace gpa {
+namespace norm {
+
+// Residual + LayerScale: out = bf16(x + bf16(y * gamma[c])), the two roundings
+// of torch's bf16 `x + y * gamma` (vggt/layers/block.py:88,94 with
+// layers/layer_scale.py:21), one pass over x and y instead of a broadcast
+// multiply followed by an add.  One thread per 8 bf16 (16-byte vectors).
+__global__ void __launch_bounds__(256) residual_scale_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t x_stride, const __nv_bfloat16* __restrict__ y,
+    int64_t y_stride, const __nv_bfloat16* __restrict__ gamma, uint32_t vec_per_row, uint32_t total,
+    __nv_bfloat16* __restrict__ out, int64_t out_stride) {
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const uint32_t r = i / vec_per_row, c = (i - r * vec_per_row) * 8;
+    const uint4 xv = *reinterpret_cast<const uint4*>(x + (int64_t)r * x_stride + c);
+    const uint4 yv = *reinterpret_cast<const uint4*>(y + (int64_t)r * y_stride + c);
+    const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gamma + c));
+    const __nv_bfloat162* xa = reinterpret_cast<const __nv_bfloat162*>(&xv);
+    const __nv_bfloat162* ya = reinterpret_cast<const __nv_bfloat162*>(&yv);
+    const __nv_bfloat162* ga = reinterpret_cast<const __nv_bfloat162*>(&gv);
+    uint4 ov;
+    __nv_bfloat162* oa = reinterpret_cast<__nv_bfloat162*>(&ov);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 xf = __bfloat1622float2(xa[k]), yf = __bfloat1622float2(ya[k]), gf = __bfloat1622float2(ga[k]);
+      const __nv_bfloat162 t = __floats2bfloat162_rn(__fmul_rn(yf.x, gf.x), __fmul_rn(yf.y, gf.y));
+      const float2 tf = __bfloat1622float2(t);
+      oa[k] = __floats2bfloat162_rn(__fadd_rn(xf.x, tf.x), __fadd_rn(xf.y, tf.y));
+    }
+    *reinterpret_cast<uint4*>(out + (int64_t)r * out_stride + c) = ov;
+  }
+}
+
+}  // namespace norm
+}  // namespace gpa
+
 using namespace gpa;
 
 extern "C" int gpa_layernorm_bf16(const void* x, int64_t x_stride, int rows, int cols,
@@ -230,4 +267,24 @@ extern "C" int gpa_qk_norm_rope(const void* qkv, int64_t token_stride, int64_t q
         eps, positions, cos_table, sin_table, n_pos, (__nv_bfloat16*)q_out, (__nv_bfloat16*)k_out,
         out_token_stride);
   return check_launch("gpa_qk_norm_rope");
+}
+
+extern "C" int gpa_residual_scale_bf16(const void* x, int64_t x_stride, const void* y, int64_t y_stride,
+                                       const void* gamma, int rows, int cols, void* out,
+                                       int64_t out_stride, void* stream) {
+  if (rows < 0 || cols <= 0 || cols % 8)
+    return fail(GPA_ERR_UNSUPPORTED, "gpa_residual_scale_bf16: cols must be a positive multiple of 8");
+  if (x_stride % 8 || y_stride % 8 || out_stride % 8 || !aligned16(x) || !aligned16(y) ||
+      !aligned16(out) || !aligned16(gamma))
+    return fail(GPA_ERR_INVALID, "gpa_residual_scale_bf16: 16-byte aligned rows and gamma required");
+  const uint64_t total = (uint64_t)rows * (uint64_t)(cols / 8);
+  if (total >= (1ull << 31))
+    return fail(GPA_ERR_UNSUPPORTED, "gpa_residual_scale_bf16: more than 2^31 vectors");
+  if (total == 0) return ok();
+  const unsigned blocks = (unsigned)std::min<uint64_t>((total + 255) / 256, 148ull * 16);
+  norm::residual_scale_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(
+      (const __nv_bfloat16*)x, x_stride, (const __nv_bfloat16*)y, y_stride,
+      (const __nv_bfloat16*)gamma, (uint32_t)(cols / 8), (uint32_t)total, (__nv_bfloat16*)out,
+      out_stride);
+  return check_launch("gpa_residual_scale_bf16");
 }

@@ -275,6 +275,30 @@ def layernorm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: fl
     return out
 
 
+def residual_scale(x: torch.Tensor, y: torch.Tensor, gamma: torch.Tensor,
+                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """x + y * gamma over the last dim, all bf16, rounded as torch's bf16 ops
+    (vggt/layers/block.py:88,94 with layer_scale.py:21) -> new bf16 tensor."""
+    require_cuda(x, y, gamma, what="residual_scale")
+    if x.dtype != BF16 or y.dtype != BF16 or gamma.dtype != BF16 or x.shape != y.shape:
+        raise ValueError("residual_scale: bf16 x, y of one shape and a bf16 gamma required")
+    C = x.shape[-1]
+    if gamma.numel() != C:
+        raise ValueError("residual_scale: gamma must have the last dim's size")
+    x2, y2 = x.reshape(-1, C), y.reshape(-1, C)
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 or not aligned(x2):
+        x2 = x2.contiguous()
+    if y2.stride(-1) != 1 or y2.stride(0) % 8 or not aligned(y2):
+        y2 = y2.contiguous()
+    g = gamma.contiguous()
+    if out is None:
+        out = torch.empty(x.shape, device=x.device, dtype=BF16)
+    o2 = out.view(-1, C)
+    call("gpa_residual_scale_bf16", ptr(x2), x2.stride(0), ptr(y2), y2.stride(0), ptr(g), x2.shape[0], C,
+         ptr(o2), o2.stride(0), stream_of(x))
+    return out
+
+
 def qk_norm_rope(qkv: torch.Tensor, q_norm, k_norm, positions: Optional[torch.Tensor],
                  cos_table: Optional[torch.Tensor], sin_table: Optional[torch.Tensor]):
     """In place on qkv [T, 3, H, 64] (bf16, contiguous): q, k <- rope(LN(q)), rope(LN(k)).

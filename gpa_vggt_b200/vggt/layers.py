@@ -385,5 +385,14 @@ class Block(nn.Module):
         self.ls2 = LayerScale(dim, init_values=init_values) if init_values else nn.Identity()
 
     def forward(self, x, pos=None, global_merging=None):
-        x = x + self.ls1(self.attn(self.norm1(x), pos=pos, global_merging=global_merging))
-        return x + self.ls2(self.mlp(self.norm2(x)))
+        x = _residual(x, self.ls1, self.attn(self.norm1(x), pos=pos, global_merging=global_merging))
+        return _residual(x, self.ls2, self.mlp(self.norm2(x)))
+
+
+def _residual(x, ls, y):
+    """x + ls(y) (vggt/layers/block.py:88,94).  With a LayerScale on CUDA bf16
+    tensors this is one fused pass (same roundings as torch's bf16 ops)."""
+    if (isinstance(ls, LayerScale) and x.is_cuda and x.dtype == BF16 and y.dtype == BF16
+            and ls.gamma.dtype == BF16 and x.shape == y.shape and x.shape[-1] % 8 == 0):
+        return kernels.residual_scale(x, y, ls.gamma)
+    return x + ls(y)

@@ -236,6 +236,17 @@ GPA_API int gpa_qk_norm_rope(const void* qkv, int64_t token_stride, int64_t q_of
                              const float* sin_table, int n_pos, void* q_out, void* k_out,
                              int64_t out_token_stride, void* stream);
 
+/*
+ * Residual + LayerScale (vggt/layers/block.py:88,94 with
+ * vggt/layers/layer_scale.py:21): out[r, c] = bf16(x[r, c] + bf16(y[r, c] * gamma[c])),
+ * rounding exactly as torch's bf16 `x + y * gamma`.  All bf16; rows of `cols`
+ * contiguous elements at the given row strides (elements); cols % 8 == 0;
+ * 16-byte aligned rows and gamma.  out may alias x.
+ */
+GPA_API int gpa_residual_scale_bf16(const void* x, int64_t x_stride, const void* y,
+                                    int64_t y_stride, const void* gamma, int rows, int cols,
+                                    void* out, int64_t out_stride, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -65,3 +65,29 @@ def test_qk_norm_rope_matches_torch_path(with_rope):
     _ulp_ok(q, qr[0].bfloat16())
     _ulp_ok(k, kr[0].bfloat16())
     assert torch.equal(v, v_before)
+
+
+@pytest.mark.parametrize("shape", [(200, 1374, 1024), (1, 3001, 1024), (7, 64)])
+def test_residual_scale_bitexact_with_torch(shape):
+    """x + y * gamma (LayerScale residual) equals torch's two bf16 ops bit for
+    bit, including a strided y (a column slice of a wider buffer)."""
+    from gpa_vggt_b200 import kernels
+    g = torch.Generator(device="cuda").manual_seed(shape[-1] + shape[0])
+    x = (torch.randn(*shape, device="cuda", generator=g) * 4).bfloat16()
+    y = (torch.randn(*shape, device="cuda", generator=g) * 50).bfloat16()
+    gamma = (0.01 * torch.randn(shape[-1], device="cuda", generator=g)).bfloat16()
+    assert torch.equal(kernels.residual_scale(x, y, gamma), x + y * gamma)
+    wide = torch.randn(*shape[:-1], shape[-1] + 16, device="cuda", generator=g).bfloat16()
+    ys = wide[..., 8:8 + shape[-1]]
+    assert torch.equal(kernels.residual_scale(x, ys, gamma), x + ys * gamma)
+
+
+def test_block_residual_uses_fused_kernel_and_matches():
+    """Block.forward's residual path with LayerScale on CUDA bf16 gives the
+    unfused expression's result exactly."""
+    from gpa_vggt_b200.vggt.layers import LayerScale, _residual
+    g = torch.Generator(device="cuda").manual_seed(3)
+    ls = LayerScale(1024, init_values=0.01).cuda().bfloat16()
+    x = torch.randn(2, 300, 1024, device="cuda", generator=g).bfloat16()
+    y = torch.randn(2, 300, 1024, device="cuda", generator=g).bfloat16()
+    assert torch.equal(_residual(x, ls, y), x + ls(y))
