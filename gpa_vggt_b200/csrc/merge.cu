@@ -105,6 +105,16 @@ struct Vec8<__nv_bfloat16> {
       v[2 * i + 1] = f.y;
     }
   }
+  static __device__ __forceinline__ void load_shared(const __nv_bfloat16* p, float* v) {
+    uint4 raw = *reinterpret_cast<const uint4*>(p);
+    const __nv_bfloat162* e = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 f = __bfloat1622float2(e[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
   static __device__ __forceinline__ void store(__nv_bfloat16* p, const float* v) {
     uint4 raw;
     __nv_bfloat162* e = reinterpret_cast<__nv_bfloat162*>(&raw);
@@ -118,6 +128,12 @@ struct Vec8<float> {
   static __device__ __forceinline__ void load(const float* p, float* v) {
     float4 a = __ldg(reinterpret_cast<const float4*>(p));
     float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+  static __device__ __forceinline__ void load_shared(const float* p, float* v) {
+    float4 a = reinterpret_cast<const float4*>(p)[0];
+    float4 b = reinterpret_cast<const float4*>(p)[1];
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
     v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
   }
@@ -404,16 +420,56 @@ __global__ void ones_f32_kernel(float* __restrict__ f, int n) {
 // ---------------------------------------------------------------------------
 // One warp per output slot; the warp's lanes cover heads*head_dim in chunks of
 // 8 elements, up to CPL chunks per lane (heads*head_dim <= CPL*256).
+//
+// The group's rows (the dst token first, then its src members in ascending
+// ordinal order) are fetched ROWS at a time with cp.async into this warp's
+// shared-memory staging area: the token positions of a batch are resolved one
+// per lane in parallel, and every row copy of the batch is in flight at once
+// without holding registers.  Warps are persistent and double-buffer their
+// batches, so the index loads and row copies of the next batch overlap the
+// wait for this one.  The fp32 sums run in the fixed row order
+// (deterministic, unlike the reference's scatter_reduce).
+#ifndef GPA_MERGE_WARPS
+#define GPA_MERGE_WARPS 2
+#endif
+#ifndef GPA_MERGE_ROWS
+#define GPA_MERGE_ROWS 2
+#endif
+constexpr int kMergeWarps = GPA_MERGE_WARPS;   // warps (persistent slot walkers) per block
+constexpr int kMergeRows = GPA_MERGE_ROWS;     // rows per staged batch (two batches per warp)
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// One batch of a slot's rows: the slot, its kept token, its members and which
+// ROWS-row batch of them.
+struct MergeItem {
+  int slot, first_tok, s0, nmem, batch;
+};
+
 template <typename T, int CPL>
-__global__ void __launch_bounds__(256) merge_mean_kernel(
+__global__ void __launch_bounds__(kMergeWarps * 32) merge_mean_kernel(
     const T* __restrict__ t, int heads, int head_dim, int64_t sh, int64_t sn,
     const int32_t* __restrict__ src_pos, const int32_t* __restrict__ dst_pos,
     const int32_t* __restrict__ unm_src, int unm_len, const int32_t* __restrict__ seg_start,
     const int32_t* __restrict__ seg_src, int num_dst, int reduce_mean,
-    float* __restrict__ log_counts, T* __restrict__ out, int64_t osh, int64_t osn) {
-  const int slot = blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (slot >= unm_len + num_dst) return;
+    float* __restrict__ log_counts, T* __restrict__ out, int64_t osh, int64_t osn, int rows_per_batch) {
+  extern __shared__ __align__(16) uint8_t merge_smem[];
+  constexpr int kChunk = 8 * (int)sizeof(T);       // bytes of 8 elements
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int slots = unm_len + num_dst;
+  const int warps_total = gridDim.x * kMergeWarps;
+  const int first_slot = blockIdx.x * kMergeWarps + warp;
+  if (first_slot >= slots) return;                 // warp-uniform
   const int cph = head_dim / 8;        // chunks per head
   const int nch = heads * cph;         // chunks per token
   int64_t in_off[CPL], out_off[CPL];
@@ -425,48 +481,110 @@ __global__ void __launch_bounds__(256) merge_mean_kernel(
     int hh = live[c] ? ch / cph : 0;
     int d0 = live[c] ? (ch - hh * cph) * 8 : 0;
     in_off[c] = (int64_t)hh * sh + d0;
-    out_off[c] = (int64_t)hh * osh + (int64_t)slot * osn + d0;
+    out_off[c] = (int64_t)hh * osh + d0;
   }
-  float acc[CPL][8];
-  if (slot < unm_len) {
-    const int64_t tok = src_pos[unm_src[slot]];
-#pragma unroll
-    for (int c = 0; c < CPL; ++c)
-      if (live[c]) {
-        Vec8<T>::load(t + tok * sn + in_off[c], acc[c]);
-        Vec8<T>::store(out + out_off[c], acc[c]);
-      }
-    if (log_counts && lane == 0) log_counts[slot] = 0.0f;
-    return;
-  }
-  const int g = slot - unm_len;
-  const int64_t dtok = dst_pos[g];
-#pragma unroll
-  for (int c = 0; c < CPL; ++c)
-    if (live[c]) Vec8<T>::load(t + dtok * sn + in_off[c], acc[c]);
-  const int s0 = seg_start[g], s1 = seg_start[g + 1];
-  for (int s = s0; s < s1; ++s) {
-    const int64_t tok = src_pos[seg_src[s]];
-#pragma unroll
-    for (int c = 0; c < CPL; ++c)
-      if (live[c]) {
-        float v[8];
-        Vec8<T>::load(t + tok * sn + in_off[c], v);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[c][i] += v[i];
-      }
-  }
-  const float cnt = (float)(1 + s1 - s0);
-#pragma unroll
-  for (int c = 0; c < CPL; ++c)
-    if (live[c]) {
-      if (reduce_mean) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[c][i] = __fdiv_rn(acc[c][i], cnt);
-      }
-      Vec8<T>::store(out + out_off[c], acc[c]);
+  const size_t stage_bytes = (size_t)rows_per_batch * nch * kChunk;
+  uint8_t* stages = merge_smem + (size_t)warp * 2 * stage_bytes;
+
+  auto load_slot = [&](int sl, MergeItem& it) {
+    it.slot = sl;
+    it.batch = 0;
+    if (sl < unm_len) {
+      it.first_tok = src_pos[unm_src[sl]];
+      it.s0 = 0;
+      it.nmem = 0;
+    } else {
+      const int g = sl - unm_len;
+      it.first_tok = dst_pos[g];
+      it.s0 = seg_start[g];
+      it.nmem = seg_start[g + 1] - it.s0;
     }
-  if (log_counts && lane == 0) log_counts[slot] = logf(cnt);
+  };
+  // the next batch of the same slot, else the first batch of this warp's next slot
+  auto advance = [&](MergeItem& it) -> bool {
+    if ((it.batch + 1) * rows_per_batch < 1 + it.nmem) {
+      ++it.batch;
+      return true;
+    }
+    const int ns = it.slot + warps_total;
+    if (ns >= slots) return false;
+    load_slot(ns, it);
+    return true;
+  };
+  // resolve the batch's token positions (one per lane) and start its row copies
+  auto issue = [&](const MergeItem& it, uint8_t* stage) {
+    const int base = it.batch * rows_per_batch;
+    const int nb = min(rows_per_batch, 1 + it.nmem - base);
+    int my_tok = 0;
+    if (lane < nb) my_tok = base + lane == 0 ? it.first_tok : src_pos[seg_src[it.s0 + base + lane - 1]];
+    for (int i = 0; i < nb; ++i) {
+      const int64_t tok = __shfl_sync(0xffffffffu, my_tok, i);
+      const uint8_t* row = reinterpret_cast<const uint8_t*>(t + tok * sn);
+#pragma unroll
+      for (int c = 0; c < CPL; ++c)
+        if (live[c]) {
+          uint8_t* dst = stage + ((size_t)i * nch + lane + c * 32) * kChunk;
+          const uint8_t* src = row + in_off[c] * (int64_t)sizeof(T);
+#pragma unroll
+          for (int q = 0; q < kChunk / 16; ++q) cp_async16(dst + q * 16, src + q * 16);
+        }
+    }
+    cp_async_commit();
+  };
+
+  float acc[CPL][8];
+#pragma unroll
+  for (int c = 0; c < CPL; ++c)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[c][i] = 0.0f;
+  MergeItem cur;
+  load_slot(first_slot, cur);
+  issue(cur, stages);
+  int buf = 0;
+  while (true) {
+    // the next batch's index loads and row copies overlap this batch's wait
+    MergeItem nxt = cur;
+    const bool more = advance(nxt);
+    if (more) {
+      issue(nxt, stages + (buf ^ 1) * stage_bytes);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    // each lane reads back only the chunks it copied
+    const uint8_t* stage = stages + buf * stage_bytes;
+    const int nb = min(rows_per_batch, 1 + cur.nmem - cur.batch * rows_per_batch);
+    for (int i = 0; i < nb; ++i) {
+#pragma unroll
+      for (int c = 0; c < CPL; ++c)
+        if (live[c]) {
+          float v[8];
+          Vec8<T>::load_shared(reinterpret_cast<const T*>(stage + ((size_t)i * nch + lane + c * 32) * kChunk), v);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[c][e] += v[e];
+        }
+    }
+    if ((cur.batch + 1) * rows_per_batch >= 1 + cur.nmem) {   // the slot's last batch
+      const bool group = cur.slot >= unm_len;
+      const float cnt = (float)(1 + cur.nmem);
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        if (live[c]) {
+          if (group && reduce_mean) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[c][i] = __fdiv_rn(acc[c][i], cnt);
+          }
+          Vec8<T>::store(out + out_off[c] + (int64_t)cur.slot * osn, acc[c]);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[c][i] = 0.0f;
+      }
+      if (log_counts && lane == 0) log_counts[cur.slot] = group ? logf(cnt) : 0.0f;
+    }
+    if (!more) break;
+    cur = nxt;
+    buf ^= 1;
+  }
 }
 
 }  // namespace gpa
@@ -650,18 +768,39 @@ extern "C" int gpa_merge_kv_mean(const void* t, int dtype, int heads, int n_toke
     return fail(GPA_ERR_INVALID, "gpa_merge_kv_mean: dtype must be f32 or bf16");
   const int nch = heads * head_dim / 8;
   const int slots = unm_len + num_dst;
-  dim3 grid((slots + 7) / 8);
   cudaStream_t st = (cudaStream_t)stream;
-#define GPA_MERGE_LAUNCH(T, CPL)                                                                 \
-  merge_mean_kernel<T, CPL><<<grid, 256, 0, st>>>(                                               \
-      (const T*)t, heads, head_dim, t_stride_h, t_stride_n, src_pos, dst_pos, unm_src, unm_len, \
-      seg_start, seg_src, num_dst, reduce_mean, log_counts, (T*)out, out_stride_h, out_stride_n)
+  // staging per warp: two batches of up to kMergeRows rows (2 was fastest in a
+  // sweep of 2-4 rows x 2-8 warps per block), at most 8 KB per batch;
+  // persistent warps, a few blocks per SM
+  const int row_bytes = nch * 8 * (dtype == GPA_DTYPE_BF16 ? 2 : 4);
+  const int rows_per_batch = std::max(1, std::min(kMergeRows, 8192 / row_bytes));
+  const size_t smem = (size_t)kMergeWarps * 2 * rows_per_batch * row_bytes;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // one wave of resident blocks (persistent warps)
+  auto grid_for = [&](const void* fn) {
+    int per_sm = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kMergeWarps * 32, smem) != cudaSuccess ||
+        per_sm < 1)
+      per_sm = 1;
+    return dim3((unsigned)std::min<int64_t>((slots + kMergeWarps - 1) / kMergeWarps, (int64_t)sms * per_sm));
+  };
+#define GPA_MERGE_LAUNCH(T, CPL)                                                                  \
+  {                                                                                              \
+    cudaFuncSetAttribute(merge_mean_kernel<T, CPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                         (int)smem);                                                             \
+    const dim3 grid = grid_for((const void*)merge_mean_kernel<T, CPL>);                          \
+    merge_mean_kernel<T, CPL><<<grid, kMergeWarps * 32, smem, st>>>(                             \
+        (const T*)t, heads, head_dim, t_stride_h, t_stride_n, src_pos, dst_pos, unm_src, unm_len, \
+        seg_start, seg_src, num_dst, reduce_mean, log_counts, (T*)out, out_stride_h, out_stride_n, \
+        rows_per_batch);                                                                         \
+  }
   if (nch <= 32) {
-    if (dtype == GPA_DTYPE_BF16) GPA_MERGE_LAUNCH(__nv_bfloat16, 1); else GPA_MERGE_LAUNCH(float, 1);
+    if (dtype == GPA_DTYPE_BF16) GPA_MERGE_LAUNCH(__nv_bfloat16, 1) else GPA_MERGE_LAUNCH(float, 1)
   } else if (nch <= 128) {
-    if (dtype == GPA_DTYPE_BF16) GPA_MERGE_LAUNCH(__nv_bfloat16, 4); else GPA_MERGE_LAUNCH(float, 4);
+    if (dtype == GPA_DTYPE_BF16) GPA_MERGE_LAUNCH(__nv_bfloat16, 4) else GPA_MERGE_LAUNCH(float, 4)
   } else if (nch <= 256) {
-    if (dtype == GPA_DTYPE_BF16) GPA_MERGE_LAUNCH(__nv_bfloat16, 8); else GPA_MERGE_LAUNCH(float, 8);
+    if (dtype == GPA_DTYPE_BF16) GPA_MERGE_LAUNCH(__nv_bfloat16, 8) else GPA_MERGE_LAUNCH(float, 8)
   } else {
     return fail(GPA_ERR_UNSUPPORTED, "gpa_merge_kv_mean: heads*head_dim > 2048");
   }

@@ -133,8 +133,9 @@ def test_merge_plan_matches_oracle(ns, nd, ratio):
 
 # ---------------------------------------------------------------- scatter-mean
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("ratio", [1.0, 0.3])
-def test_merge_kv_matches_oracle(dtype, ratio):
+@pytest.mark.parametrize("ratio,hub", [(1.0, False), (0.3, False), (1.0, True)])
+def test_merge_kv_matches_oracle(dtype, ratio, hub):
+    """hub: one dst receives 300 members (staged in several row batches)."""
     from gpa_vggt_b200 import kernels
     g = torch.Generator().manual_seed(5)
     S, w, h, ns_, H, D = 4, 37, 37, 5, 16, 64
@@ -145,6 +146,8 @@ def test_merge_kv_matches_oracle(dtype, ratio):
     dst, src = O.split_positions(mask)
     node_max = torch.rand(src.numel(), generator=g)
     node_idx = torch.randint(0, dst.numel(), (src.numel(),), generator=g)
+    if hub:
+        node_idx[::10] = 7
     r = int(N * ratio)
     t = torch.randn(H, N, D, generator=g).to(dtype)
     plan = kernels.merge_plan(node_max.to(DEV), node_idx.int().to(DEV), r, dst.int().to(DEV),
