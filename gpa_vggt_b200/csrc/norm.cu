@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const __nv_bfloat16* __r
   }
 }
 
-// One thread per 64-wide head row of q or k.  Rotary layout: dims 0..31 turn
+// Per 64-wide head row of q or k.  Rotary layout: dims 0..31 turn
 // with the row coordinate, 32..63 with the column coordinate; inside each half
 // the rotate-half pairing (i, i+16).  cos/sin tables: [n_pos, 32] fp32.
 template <typename W>
@@ -88,74 +88,78 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     const W* __restrict__ kw, const W* __restrict__ kb, float eps, const int64_t* __restrict__ pos,
     const float* __restrict__ cos_tab, const float* __restrict__ sin_tab, int n_pos,
     __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_out, int64_t out_tok_stride) {
-  __shared__ float s_w[2][64], s_b[2][64];
-  if (threadIdx.x < 64) {
-    s_w[0][threadIdx.x] = qw ? ldw(qw, threadIdx.x) : 1.f;
-    s_b[0][threadIdx.x] = qb ? ldw(qb, threadIdx.x) : 0.f;
-    s_w[1][threadIdx.x] = kw ? ldw(kw, threadIdx.x) : 1.f;
-    s_b[1][threadIdx.x] = kb ? ldw(kb, threadIdx.x) : 0.f;
-  }
-  __syncthreads();
-  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  // 8 lanes per 64-wide head row, 8 consecutive features per lane: 16-byte
+  // coalesced loads and stores, mean/variance by xor-shuffles inside the
+  // 8-lane group, the rotate-half partner (feature i +- 16) in lane ^ 2.
   const int64_t per = (int64_t)tokens * heads;
-  if (gid >= 2 * per) return;
-  const int which = gid >= per;  // 0 = q, 1 = k
-  const int64_t r = gid - which * per;
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
+  if (row >= 2 * per) return;          // whole 8-lane groups leave together
+  const int lane = threadIdx.x & 31, sub = lane & 7;
+  const unsigned gmask = 0xffu << (lane & 24);
+  const int which = row >= per;        // 0 = q, 1 = k
+  const int64_t r = row - which * per;
   const int64_t tok = r / heads;
   const int hh = (int)(r - tok * heads);
-  const __nv_bfloat16* src = qkv + tok * tok_stride + (which ? k_off : q_off) + hh * 64;
-  float v[64];
-  float s = 0.f;
-#pragma unroll
-  for (int u = 0; u < 8; ++u) {
-    uint4 raw = reinterpret_cast<const uint4*>(src)[u];  // may be rewritten in place: no nc path
+  const __nv_bfloat16* src = qkv + tok * tok_stride + (which ? k_off : q_off) + hh * 64 + sub * 8;
+  float v[8];
+  {
+    const uint4 raw = *reinterpret_cast<const uint4*>(src);  // may be rewritten in place: no nc path
     const __nv_bfloat162* e = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      float2 f = __bfloat1622float2(e[i]);
-      v[8 * u + 2 * i] = f.x;
-      v[8 * u + 2 * i + 1] = f.y;
-      s += f.x + f.y;
+      const float2 f = __bfloat1622float2(e[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
     }
   }
+  float s = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+  s += __shfl_xor_sync(gmask, s, 1);
+  s += __shfl_xor_sync(gmask, s, 2);
+  s += __shfl_xor_sync(gmask, s, 4);
   const float mean = s * (1.f / 64.f);
   float q = 0.f;
 #pragma unroll
-  for (int i = 0; i < 64; ++i) {
+  for (int i = 0; i < 8; ++i) {
     const float d = v[i] - mean;
     q = fmaf(d, d, q);
   }
+  q += __shfl_xor_sync(gmask, q, 1);
+  q += __shfl_xor_sync(gmask, q, 2);
+  q += __shfl_xor_sync(gmask, q, 4);
   const float rstd = rsqrtf(q * (1.f / 64.f) + eps);
+  const W* w = which ? kw : qw;
+  const W* b = which ? kb : qb;
 #pragma unroll
-  for (int i = 0; i < 64; ++i) v[i] = fmaf((v[i] - mean) * rstd, s_w[which][i], s_b[which][i]);
+  for (int i = 0; i < 8; ++i) {
+    const int f = sub * 8 + i;
+    v[i] = fmaf((v[i] - mean) * rstd, w ? ldw(w, f) : 1.f, b ? ldw(b, f) : 0.f);
+  }
   if (pos) {
+    const int half = sub >> 2, within = (sub & 3) * 8;   // feature offset inside the half
+    int p = (int)pos[tok * 2 + half];
+    p = min(max(p, 0), n_pos - 1);
+    const float4* c4 = reinterpret_cast<const float4*>(cos_tab + (int64_t)p * 32 + within);
+    const float4* s4 = reinterpret_cast<const float4*>(sin_tab + (int64_t)p * 32 + within);
+    const float4 ca = __ldg(c4), cb = __ldg(c4 + 1), sa = __ldg(s4), sb = __ldg(s4 + 1);
+    const float c[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+    const float sn[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+    const bool lower = within < 16;   // features 0..15 pair with +16, 16..31 with -16
+    float o[8];
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      int p = (int)pos[tok * 2 + half];
-      p = min(max(p, 0), n_pos - 1);
-      const float* c = cos_tab + (int64_t)p * 32;
-      const float* sn = sin_tab + (int64_t)p * 32;
-      float* t = v + half * 32;
-      float o[32];
+    for (int i = 0; i < 8; ++i) {
+      const float partner = __shfl_xor_sync(gmask, v[i], 2);
       // separate roundings of the two products and the sum, as t*cos + rot(t)*sin
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        o[i] = __fadd_rn(__fmul_rn(t[i], c[i]), __fmul_rn(-t[i + 16], sn[i]));
-        o[i + 16] = __fadd_rn(__fmul_rn(t[i + 16], c[i + 16]), __fmul_rn(t[i], sn[i + 16]));
-      }
-#pragma unroll
-      for (int i = 0; i < 32; ++i) t[i] = o[i];
+      o[i] = __fadd_rn(__fmul_rn(v[i], c[i]), __fmul_rn(lower ? -partner : partner, sn[i]));
     }
-  }
-  __nv_bfloat16* dst = (which ? k_out : q_out) + tok * out_tok_stride + hh * 64;
 #pragma unroll
-  for (int u = 0; u < 8; ++u) {
-    uint4 raw;
-    __nv_bfloat162* e = reinterpret_cast<__nv_bfloat162*>(&raw);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) e[i] = __floats2bfloat162_rn(v[8 * u + 2 * i], v[8 * u + 2 * i + 1]);
-    reinterpret_cast<uint4*>(dst)[u] = raw;
+    for (int i = 0; i < 8; ++i) v[i] = o[i];
   }
+  __nv_bfloat16* dst = (which ? k_out : q_out) + tok * out_tok_stride + hh * 64 + sub * 8;
+  uint4 raw;
+  __nv_bfloat162* e = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) e[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(dst) = raw;
 }
 
 }  // namespace norm
@@ -248,11 +252,13 @@ extern "C" int gpa_qk_norm_rope(const void* qkv, int64_t token_stride, int64_t q
     return fail(GPA_ERR_INVALID, "gpa_qk_norm_rope: 16-byte aligned rows required");
   if (positions && (!cos_table || !sin_table || n_pos <= 0))
     return fail(GPA_ERR_INVALID, "gpa_qk_norm_rope: rotary tables missing");
+  if (positions && (!aligned16(cos_table) || !aligned16(sin_table)))
+    return fail(GPA_ERR_INVALID, "gpa_qk_norm_rope: rotary tables must be 16-byte aligned");
   if (param_dtype != GPA_DTYPE_F32 && param_dtype != GPA_DTYPE_BF16)
     return fail(GPA_ERR_INVALID, "gpa_qk_norm_rope: weight dtype must be f32 or bf16");
   const int64_t rows = 2ll * tokens * heads;
   if (rows == 0) return ok();
-  const unsigned blocks = (unsigned)((rows + 255) / 256);
+  const unsigned blocks = (unsigned)((rows * 8 + 255) / 256);   // 8 lanes per row
   cudaStream_t st = (cudaStream_t)stream;
   if (param_dtype == GPA_DTYPE_BF16)
     norm::qk_norm_rope_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
