@@ -293,20 +293,38 @@ __device__ __forceinline__ void regs_inc() {
 }
 
 // Packed fp32 pairs (sm_100): one instruction for two lanes of math.
+// Packed fp32x2 FMA / add (sm_100), as inline PTX.  GPA_F2_ASM=0 selects the
+// compiler intrinsics (__ffma2_rn / __fadd2_rn) instead, which measured about
+// 0.6% slower in the attention kernel.
+#ifndef GPA_F2_ASM
+#define GPA_F2_ASM 1
+#endif
 __device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1,
                                       float c0, float c1) {
+#if GPA_F2_ASM
   asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
       "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
       "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
       : "=f"(d0), "=f"(d1)
       : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+#else
+  const float2 r = __ffma2_rn(make_float2(a0, a1), make_float2(b0, b1), make_float2(c0, c1));
+  d0 = r.x;
+  d1 = r.y;
+#endif
 }
 __device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+#if GPA_F2_ASM
   asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
       "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
       "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
       : "=f"(d0), "=f"(d1)
       : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+#else
+  const float2 r = __fadd2_rn(make_float2(a0, a1), make_float2(b0, b1));
+  d0 = r.x;
+  d1 = r.y;
+#endif
 }
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
