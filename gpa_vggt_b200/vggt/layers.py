@@ -242,6 +242,16 @@ def merged_attention_sharded(x, q, k, v, attn: Attention) -> torch.Tensor:
     if Nl != sh.local * P:
         raise ValueError("merged_attention_sharded: local tokens do not match the frame shard")
     dev = x.device
+    # the key/value exchange (the bulk of the bytes) starts first and overlaps
+    # the matching below; K and V travel as one [N, 2, H, D] buffer
+    if k.dtype == v.dtype:
+        kv_full, kv_work = sh.gather_async(torch.stack((k[0], v[0]), 1))
+        k_full, v_full = kv_full[:, 0], kv_full[:, 1]
+        works = (kv_work,)
+    else:   # fp32 K (unfused qk path) and bf16 V: two exchanges
+        k_full, kw = sh.gather_async(k[0])
+        v_full, vw = sh.gather_async(v[0])
+        works = (kw, vw)
     rand_idx, proj = _merge_draws(attn, S, C, dev, x.dtype)
     dst_pos, src_pos, _ = kernels.merge_roles(rand_idx, S, pw, ph, g, g, ns, False, dev)
     dpf = ns + (ph // g) * (pw // g)
@@ -263,9 +273,9 @@ def merged_attention_sharded(x, q, k, v, attn: Attention) -> torch.Tensor:
     nm_full = sh.gather_varlen(nm, src_counts)
     ni_full = sh.gather_varlen(ni, src_counts)
     plan = kernels.merge_plan(nm_full, ni_full, int(N * attn.merge_ratio), dst_pos, src_pos)
-    k_full = sh.gather(k[0].contiguous())                       # [N, H, D]
-    v_full = sh.gather(v[0].contiguous())
-    km = kernels.merge_kv(k_full.transpose(0, 1), plan)
+    for w in works:
+        w.wait()
+    km = kernels.merge_kv(k_full.transpose(0, 1), plan)   # [H, N, D] (strided) views
     vm = kernels.merge_kv(v_full.transpose(0, 1), plan)
     bias = plan.counts.log().to(BF16).float()
     out = torch.empty(1, Nl, H, D, device=dev, dtype=BF16)

@@ -35,6 +35,13 @@ class FrameShard:
         self.local = frames // self.world
         self.f0 = self.rank * self.local
         self.f1 = self.f0 + self.local
+        # a second communicator for the bulk key/value exchange, so it runs on its
+        # own stream while the small match-result gathers and kernels proceed
+        # (every rank constructs the shard, so every rank joins the new group)
+        self.kv_group = None
+        if self.world > 1:
+            ranks = dist.get_process_group_ranks(group) if group is not None else list(range(self.world))
+            self.kv_group = dist.new_group(ranks)
 
     @property
     def active(self) -> bool:
@@ -46,6 +53,15 @@ class FrameShard:
         out = torch.empty((self.world * t.shape[0],) + tuple(t.shape[1:]), device=t.device, dtype=t.dtype)
         dist.all_gather_into_tensor(out, t, group=self.group)
         return out
+
+    def gather_async(self, t: torch.Tensor):
+        """Start an all-gather of equal-size tensors along dim 0 on the key/value
+        communicator; returns (output, work).  work.wait() orders the current
+        stream after the exchange."""
+        t = t.contiguous()
+        out = torch.empty((self.world * t.shape[0],) + tuple(t.shape[1:]), device=t.device, dtype=t.dtype)
+        work = dist.all_gather_into_tensor(out, t, group=self.kv_group, async_op=True)
+        return out, work
 
     def gather_varlen(self, t: torch.Tensor, counts: Sequence[int]) -> torch.Tensor:
         """All-gather along dim 0 when rank i holds counts[i] rows."""
