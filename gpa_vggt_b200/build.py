@@ -21,7 +21,7 @@ CSRC = PKG / "csrc"
 LIB = PKG / "libgpa_b200.so"
 HEADER = ROOT / "include" / "gpa_b200.h"
 
-SOURCES = ["merge.cu", "sim_argmax.cu", "attention.cu", "frame.cu", "norm.cu"]
+SOURCES = ["merge.cu", "sim_argmax.cu", "attention.cu", "frame.cu", "norm.cu", "dpt.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",

@@ -275,6 +275,31 @@ def layernorm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: fl
     return out
 
 
+def upsample_bilinear_bf16(x: torch.Tensor, size, add: Optional[torch.Tensor] = None,
+                           round_first: bool = False) -> torch.Tensor:
+    """bf16(bilinear_align_corners(x) [+ add]) for an fp32 or bf16 [N, C, H, W]
+    map in channels-last memory, computed in fp32; add is fp32 [1, C, OH, OW]
+    (channel stride 1), added after rounding the resize to bf16 when
+    round_first.  Returns a bf16 channels-last [N, C, OH, OW] tensor
+    (dpt_head.py custom_interpolate, _apply_pos_embed, with the next autocast
+    conv's input cast)."""
+    require_cuda(x, what="upsample_bilinear_bf16")
+    N, C, H, W = x.shape
+    OH, OW = int(size[0]), int(size[1])
+    if x.dtype not in (torch.float32, BF16) or x.stride(1) != 1:
+        raise ValueError("upsample_bilinear_bf16: fp32/bf16 channels-last input required")
+    out = torch.empty((N, OH, OW, C), device=x.device, dtype=BF16).permute(0, 3, 1, 2)
+    a_sh = a_sw = 0
+    if add is not None:
+        if add.dtype != torch.float32 or tuple(add.shape[-3:]) != (C, OH, OW) or add.stride(-3) != 1:
+            raise ValueError("upsample_bilinear_bf16: add must be fp32 [1, C, OH, OW] with channel stride 1")
+        a_sh, a_sw = add.stride(-2), add.stride(-1)
+    call("gpa_upsample_bilinear_bf16", ptr(x), _dt(x), N, C, H, W, x.stride(0), x.stride(2), x.stride(3),
+         ptr(add), a_sh, a_sw, int(round_first), OH, OW, ptr(out), out.stride(0), out.stride(2),
+         out.stride(3), stream_of(x))
+    return out
+
+
 def residual_scale(x: torch.Tensor, y: torch.Tensor, gamma: torch.Tensor,
                    out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """x + y * gamma over the last dim, all bf16, rounded as torch's bf16 ops

@@ -10,6 +10,8 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from .. import kernels
+
 from .layers import Block, LayerNorm, Mlp, SdpaAttention
 
 
@@ -91,6 +93,29 @@ def _interp(x, size=None, scale_factor=None, mode="bilinear", align_corners=True
     return F.interpolate(x, size=size, mode=mode, align_corners=align_corners)
 
 
+_RESIZE_FP32: dict = {}
+
+
+def _autocast_resize_in_fp32(device) -> bool:
+    """Whether bf16 autocast runs a bilinear resize of a bf16 map in fp32 (and
+    returns fp32); probed once per device."""
+    key = (device.type, device.index)
+    if key not in _RESIZE_FP32:
+        with torch.autocast(device.type, dtype=torch.bfloat16):
+            y = F.interpolate(torch.zeros(1, 8, 2, 2, device=device, dtype=torch.bfloat16), size=(3, 3),
+                              mode="bilinear", align_corners=True)
+        _RESIZE_FP32[key] = y.dtype == torch.float32
+    return _RESIZE_FP32[key]
+
+
+def _fused_resize_ok(x) -> bool:
+    """The resize feeds an autocast bf16 convolution and the map is channels-last
+    on CUDA: the fused resize kernel gives that convolution the same input."""
+    return (x.is_cuda and x.dim() == 4 and x.dtype in (torch.bfloat16, torch.float32)
+            and torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16
+            and x.stride(1) == 1 and x.shape[1] % 8 == 0)
+
+
 class ResidualConvUnit(nn.Module):
     """conv2(relu(conv1(relu(x)))) + relu(x): the reference's activation is an
     in-place ReLU applied to the unit's input, so its skip connection carries
@@ -120,7 +145,12 @@ class FeatureFusionBlock(nn.Module):
         if self.has_residual:
             out = out + self.resConfUnit1(xs[1])
         out = self.resConfUnit2(out)
-        out = _interp(out, size=size) if size is not None else _interp(out, scale_factor=2)
+        if size is None:
+            size = (int(out.shape[-2] * 2), int(out.shape[-1] * 2))
+        if _fused_resize_ok(out):   # resize + the conv's bf16 input cast, one pass
+            out = kernels.upsample_bilinear_bf16(out, size)
+        else:
+            out = _interp(out, size=size)
         return self.out_conv(out)
 
 
@@ -151,14 +181,19 @@ class DPTHead(nn.Module):
         self.scratch = sc
         self._pe = {}
 
-    def _pos(self, x, W, H, ratio=0.1):
-        key = (x.shape[1], x.shape[2], x.shape[3], x.dtype, str(x.device), W, H)
+    def _pe_map(self, C, h, w, dtype, device, W, H, ratio=0.1):
+        """The fp32 positional map [1, C, h, w] (channel stride 1) for a map of
+        `dtype` (the uv grid is built in that dtype, as the reference does)."""
+        key = (C, h, w, dtype, str(device), W, H)
         pe = self._pe.get(key)
         if pe is None:
-            grid = _uv_grid(x.shape[-1], x.shape[-2], W / H, x.dtype, x.device)
-            pe = (_grid_embed(grid, x.shape[1]) * ratio).permute(2, 0, 1)[None]  # fp32, as the reference
+            grid = _uv_grid(w, h, W / H, dtype, device)
+            pe = (_grid_embed(grid, C) * ratio).permute(2, 0, 1)[None]  # fp32, as the reference
             self._pe[key] = pe
-        return x + pe
+        return pe
+
+    def _pos(self, x, W, H):
+        return x + self._pe_map(x.shape[1], x.shape[2], x.shape[3], x.dtype, x.device, W, H)
 
     def _chunk(self, taps, images, psi, f0, f1):
         imgs = images[:, f0:f1]
@@ -177,8 +212,17 @@ class DPTHead(nn.Module):
         out = sc.refinenet2(out, l2, size=l1.shape[2:])
         out = sc.refinenet1(out, l1)
         out = sc.output_conv1(out)
-        out = _interp(out, size=(ph * self.patch_size, pw * self.patch_size))
-        out = sc.output_conv2(self._pos(out, W, H))
+        size = (ph * self.patch_size, pw * self.patch_size)
+        if _fused_resize_ok(out):
+            # resize, the fp32 positional add and the conv's bf16 input cast in one
+            # pass; the add sees the resize's own dtype under autocast
+            fp32 = _autocast_resize_in_fp32(out.device)
+            pe = self._pe_map(out.shape[1], size[0], size[1], torch.float32 if fp32 else out.dtype,
+                              out.device, W, H)
+            out = sc.output_conv2(kernels.upsample_bilinear_bf16(out, size, add=pe, round_first=not fp32))
+        else:
+            out = _interp(out, size=size)
+            out = sc.output_conv2(self._pos(out, W, H))
         fmap = out.permute(0, 2, 3, 1)
         depth = torch.exp(fmap[..., :-1])          # activation "exp"
         conf = 1 + fmap[..., -1].exp()             # conf_activation "expp1"

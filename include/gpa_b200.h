@@ -247,6 +247,23 @@ GPA_API int gpa_residual_scale_bf16(const void* x, int64_t x_stride, const void*
                                     int64_t y_stride, const void* gamma, int rows, int cols,
                                     void* out, int64_t out_stride, void* stream);
 
+/*
+ * DPT head resize (heads/dpt_head.py custom_interpolate -> out_conv /
+ * output_conv2, and _apply_pos_embed): bilinear, align_corners=True, in fp32,
+ * of a channels-last map x [n, c, h, w] of dtype x_dtype (f32 or bf16;
+ * element strides x_sn, x_sh, x_sw; channel stride 1) to out_h x out_w.
+ * Optionally adds an fp32 map add[c, out_h, out_w] (strides add_sh, add_sw;
+ * channel stride 1, broadcast over n), after rounding the resize to bf16 first
+ * when round_first != 0; writes bf16 channels-last out: the value a
+ * bf16-autocast convolution receives after the reference's resize (and add).
+ * c % 8 == 0; 16-byte aligned pixels.
+ */
+GPA_API int gpa_upsample_bilinear_bf16(const void* x, int x_dtype, int n, int c, int h, int w,
+                                       int64_t x_sn, int64_t x_sh, int64_t x_sw, const float* add,
+                                       int64_t add_sh, int64_t add_sw, int round_first, int out_h,
+                                       int out_w, void* out, int64_t out_sn, int64_t out_sh,
+                                       int64_t out_sw, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
