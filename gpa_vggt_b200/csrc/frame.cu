@@ -140,34 +140,46 @@ __global__ void __launch_bounds__(256) pool_kernel(const __nv_bfloat16* __restri
 
 // One warp per row: o = bf16(bf16(oa*ca) + ob*cb) with ca, cb the normalised
 // partition weights rounded to bf16, as the reference's in-place mul_/addcmul_.
-__global__ void combine_kernel(int heads, int frames, int rows, const __nv_bfloat16* __restrict__ oa,
-                               int64_t a0, int64_t a1, int64_t a2, const float* __restrict__ la,
-                               int64_t la0, int64_t la1, int64_t la2,
-                               const __nv_bfloat16* __restrict__ ob, int64_t b0, int64_t b1,
-                               int64_t b2, const float* __restrict__ lb, int64_t lb0, int64_t lb1,
-                               int64_t lb2, __nv_bfloat16* __restrict__ o, int64_t o0, int64_t o1,
-                               int64_t o2) {
-  const int64_t gid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
+__global__ void __launch_bounds__(256) combine_kernel(
+    int heads, int frames, int rows, const __nv_bfloat16* __restrict__ oa, int64_t a0, int64_t a1,
+    int64_t a2, const float* __restrict__ la, int64_t la0, int64_t la1, int64_t la2,
+    const __nv_bfloat16* __restrict__ ob, int64_t b0, int64_t b1, int64_t b2,
+    const float* __restrict__ lb, int64_t lb0, int64_t lb1, int64_t lb2, __nv_bfloat16* __restrict__ o,
+    int64_t o0, int64_t o1, int64_t o2) {
+  // 8 lanes per 64-wide (frame, row, head) row, 8 features (16 bytes) per lane;
+  // rows walk (frame, row, head) so token-major tensors stream in memory order
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t total = (int64_t)heads * frames * rows;
-  if (gid >= total) return;
-  const int r = (int)(gid % rows);
-  const int s = (int)((gid / rows) % frames);
-  const int hh = (int)(gid / ((int64_t)rows * frames));
-  const float xa = la[hh * la0 + s * la1 + r * la2];
-  const float xb = lb[hh * lb0 + s * lb1 + r * lb2];
+  const int64_t row = gid >> 3;
+  if (row >= total) return;
+  const int sub = (int)(gid & 7);
+  const int hh = (int)(row % heads);
+  const int64_t sr = row / heads;
+  const int r = (int)(sr % rows);
+  const int s = (int)(sr / rows);
+  const float xa = __ldg(la + hh * la0 + s * la1 + r * la2);
+  const float xb = __ldg(lb + hh * lb0 + s * lb1 + r * lb2);
   const float mx = fmaxf(xa, xb);
   const float wa = exp2f(xa - mx), wb = exp2f(xb - mx);
   const float den = wa + wb;
+  // weights rounded to bf16, a*ca rounded to bf16, then + b*cb: the bf16
+  // tensor ops of attention.py:164-176
   const float ca = __bfloat162float(__float2bfloat16_rn(wa / den));
   const float cb = __bfloat162float(__float2bfloat16_rn(wb / den));
-  const __nv_bfloat162 va = reinterpret_cast<const __nv_bfloat162*>(oa + hh * a0 + s * a1 + r * a2)[lane];
-  const __nv_bfloat162 vb = reinterpret_cast<const __nv_bfloat162*>(ob + hh * b0 + s * b1 + r * b2)[lane];
-  float2 fa = __bfloat1622float2(va), fb = __bfloat1622float2(vb);
-  float t0 = __bfloat162float(__float2bfloat16_rn(fa.x * ca));
-  float t1 = __bfloat162float(__float2bfloat16_rn(fa.y * ca));
-  reinterpret_cast<__nv_bfloat162*>(o + hh * o0 + s * o1 + r * o2)[lane] =
-      __floats2bfloat162_rn(t0 + fb.x * cb, t1 + fb.y * cb);
+  const uint4 va = __ldg(reinterpret_cast<const uint4*>(oa + hh * a0 + s * a1 + r * a2 + sub * 8));
+  const uint4 vb = __ldg(reinterpret_cast<const uint4*>(ob + hh * b0 + s * b1 + r * b2 + sub * 8));
+  const __nv_bfloat162* ea = reinterpret_cast<const __nv_bfloat162*>(&va);
+  const __nv_bfloat162* eb = reinterpret_cast<const __nv_bfloat162*>(&vb);
+  uint4 vo;
+  __nv_bfloat162* eo = reinterpret_cast<__nv_bfloat162*>(&vo);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 fa = __bfloat1622float2(ea[k]), fb = __bfloat1622float2(eb[k]);
+    const float t0 = __bfloat162float(__float2bfloat16_rn(fa.x * ca));
+    const float t1 = __bfloat162float(__float2bfloat16_rn(fa.y * ca));
+    eo[k] = __floats2bfloat162_rn(t0 + fb.x * cb, t1 + fb.y * cb);
+  }
+  *reinterpret_cast<uint4*>(o + hh * o0 + s * o1 + r * o2 + sub * 8) = vo;
 }
 
 }  // namespace frame
@@ -205,10 +217,13 @@ extern "C" int gpa_lse_combine(int heads, int frames, int rows_per_frame, int he
       !las || !bs || !lbs || !os)
     return fail(GPA_ERR_INVALID, "gpa_lse_combine: bad arguments");
   for (int i = 0; i < 3; ++i)
-    if (as[i] % 2 || bs[i] % 2 || os[i] % 2)
-      return fail(GPA_ERR_INVALID, "gpa_lse_combine: row strides must be even");
+    if (as[i] % 8 || bs[i] % 8 || os[i] % 8)
+      return fail(GPA_ERR_INVALID, "gpa_lse_combine: strides must be multiples of 8 elements");
+  if (!aligned16(oa) || !aligned16(ob) || !aligned16(o))
+    return fail(GPA_ERR_INVALID, "gpa_lse_combine: 16-byte aligned rows required");
   const int64_t total = (int64_t)heads * frames * rows_per_frame;
-  const int64_t blocks = (total + 7) / 8;
+  const int64_t blocks = (total * 8 + 255) / 256;   // 8 lanes per row
+  if (blocks > 0x7fffffffll) return fail(GPA_ERR_UNSUPPORTED, "gpa_lse_combine: too large");
   frame::combine_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
       heads, frames, rows_per_frame, (const __nv_bfloat16*)oa, as[0], as[1], as[2], la, las[0],
       las[1], las[2], (const __nv_bfloat16*)ob, bs[0], bs[1], bs[2], lb, lbs[0], lbs[1], lbs[2],
