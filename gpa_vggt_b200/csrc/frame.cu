@@ -108,10 +108,7 @@ __global__ void __launch_bounds__(256) pool_kernel(const __nv_bfloat16* __restri
   for (int w = threadIdx.x; w < npool * (HD / 8); w += blockDim.x) {
     const int g = w >> 3, c = w & 7;
     float ak[8] = {0}, av[8] = {0};
-    for (int o = gstart[g]; o < gstart[g + 1]; ++o) {
-      const int64_t tok = order[o];
-      uint4 rk = __ldg(reinterpret_cast<const uint4*>(kb + tok * sn) + c);
-      uint4 rv = __ldg(reinterpret_cast<const uint4*>(vb + tok * sn) + c);
+    auto accumulate = [&](const uint4& rk, const uint4& rv) {
       const __nv_bfloat162* ek = reinterpret_cast<const __nv_bfloat162*>(&rk);
       const __nv_bfloat162* ev = reinterpret_cast<const __nv_bfloat162*>(&rv);
 #pragma unroll
@@ -120,6 +117,25 @@ __global__ void __launch_bounds__(256) pool_kernel(const __nv_bfloat16* __restri
         ak[2 * q] += fk.x; ak[2 * q + 1] += fk.y;
         av[2 * q] += fv.x; av[2 * q + 1] += fv.y;
       }
+    };
+    // member rows four at a time (loads in flight together), summed in order
+    const int o0 = gstart[g], o1 = gstart[g + 1];
+    int o = o0;
+    for (; o + 4 <= o1; o += 4) {
+      uint4 rk[4], rv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t tok = order[o + u];
+        rk[u] = __ldg(reinterpret_cast<const uint4*>(kb + tok * sn) + c);
+        rv[u] = __ldg(reinterpret_cast<const uint4*>(vb + tok * sn) + c);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) accumulate(rk[u], rv[u]);
+    }
+    for (; o < o1; ++o) {
+      const int64_t tok = order[o];
+      accumulate(__ldg(reinterpret_cast<const uint4*>(kb + tok * sn) + c),
+                 __ldg(reinterpret_cast<const uint4*>(vb + tok * sn) + c));
     }
     const float cnt = (float)gcount[g];
     const float den = fmaxf(cnt, 1.0f);
