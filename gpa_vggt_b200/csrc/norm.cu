@@ -8,6 +8,7 @@
 //    instead of the norm, rotate, concatenate and cast kernels.
 //  * gpa_residual_scale_bf16: the residual add of a LayerScale branch,
 //    x + y * gamma, in one pass (vggt/layers/block.py:88,94).
+//  * gpa_gelu_bf16: the MLP's exact GELU on bf16 activations.
 #include "common.cuh"
 #include "capi_util.h"
 
@@ -197,6 +198,29 @@ __global__ void __launch_bounds__(256) residual_scale_kernel(
   }
 }
 
+// Exact (erf) GELU of bf16 values, computed as torch does for bf16 tensors:
+// fp32 0.5 * x * (1 + erf(x / sqrt(2))) rounded to bf16 (vggt/layers/mlp.py
+// with nn.GELU()).  16-byte vectors, grid-stride.
+__global__ void __launch_bounds__(256) gelu_kernel(const __nv_bfloat16* __restrict__ x,
+                                                   __nv_bfloat16* __restrict__ out, int64_t nvec) {
+  const float kInvSqrt2 = 0.70710678118654752440f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(x) + i);
+    const __nv_bfloat162* e = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    uint4 o;
+    __nv_bfloat162* oe = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __bfloat1622float2(e[k]);
+      const float g0 = 0.5f * f.x * (1.0f + erff(f.x * kInvSqrt2));
+      const float g1 = 0.5f * f.y * (1.0f + erff(f.y * kInvSqrt2));
+      oe[k] = __floats2bfloat162_rn(g0, g1);
+    }
+    reinterpret_cast<uint4*>(out)[i] = o;
+  }
+}
+
 }  // namespace norm
 }  // namespace gpa
 
@@ -293,4 +317,15 @@ extern "C" int gpa_residual_scale_bf16(const void* x, int64_t x_stride, const vo
       (const __nv_bfloat16*)gamma, (uint32_t)(cols / 8), (uint32_t)total, (__nv_bfloat16*)out,
       out_stride);
   return check_launch("gpa_residual_scale_bf16");
+}
+
+extern "C" int gpa_gelu_bf16(const void* x, int64_t n, void* out, void* stream) {
+  if (n < 0 || n % 8)
+    return fail(GPA_ERR_UNSUPPORTED, "gpa_gelu_bf16: element count must be a multiple of 8");
+  if (!aligned16(x) || !aligned16(out)) return fail(GPA_ERR_INVALID, "gpa_gelu_bf16: 16-byte aligned buffers required");
+  const int64_t nvec = n / 8;
+  if (nvec == 0) return ok();
+  const unsigned blocks = (unsigned)std::min<int64_t>((nvec + 255) / 256, 148ll * 32);
+  norm::gelu_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>((const __nv_bfloat16*)x, (__nv_bfloat16*)out, nvec);
+  return check_launch("gpa_gelu_bf16");
 }

@@ -300,6 +300,17 @@ def upsample_bilinear_bf16(x: torch.Tensor, size, add: Optional[torch.Tensor] = 
     return out
 
 
+def gelu(x: torch.Tensor) -> torch.Tensor:
+    """Exact GELU of a bf16 tensor, as torch computes it for bf16 -> new tensor."""
+    require_cuda(x, what="gelu")
+    if x.dtype != BF16:
+        raise ValueError("gelu: bf16 input required")
+    xc = x.contiguous()
+    out = torch.empty_like(xc)
+    call("gpa_gelu_bf16", ptr(xc), xc.numel(), ptr(out), stream_of(xc))
+    return out
+
+
 def residual_scale(x: torch.Tensor, y: torch.Tensor, gamma: torch.Tensor,
                    out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """x + y * gamma over the last dim, all bf16, rounded as torch's bf16 ops

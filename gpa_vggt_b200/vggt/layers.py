@@ -48,7 +48,13 @@ class Mlp(nn.Module):
         self.fc2 = nn.Linear(hidden_features, out_features, bias=bias)
 
     def forward(self, x):
-        return self.fc2(self.act(self.fc1(x)))
+        h = self.fc1(x)
+        if (isinstance(self.act, nn.GELU) and self.act.approximate == "none" and h.is_cuda
+                and h.dtype == BF16 and h.numel() % 8 == 0):
+            h = kernels.gelu(h)   # same fp32 erf expression, one vectorised pass
+        else:
+            h = self.act(h)
+        return self.fc2(h)
 
 
 class LayerScale(nn.Module):

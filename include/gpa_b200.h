@@ -264,6 +264,13 @@ GPA_API int gpa_upsample_bilinear_bf16(const void* x, int x_dtype, int n, int c,
                                        int out_w, void* out, int64_t out_sn, int64_t out_sh,
                                        int64_t out_sw, void* stream);
 
+/*
+ * Exact GELU of the MLP (vggt/layers/mlp.py, nn.GELU()): out[i] =
+ * bf16(0.5 * x * (1 + erf(x / sqrt(2)))) in fp32 for n bf16 values, as torch
+ * evaluates it for bf16 tensors.  n % 8 == 0, 16-byte aligned; out may alias x.
+ */
+GPA_API int gpa_gelu_bf16(const void* x, int64_t n, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

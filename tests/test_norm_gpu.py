@@ -91,3 +91,25 @@ def test_block_residual_uses_fused_kernel_and_matches():
     x = torch.randn(2, 300, 1024, device="cuda", generator=g).bfloat16()
     y = torch.randn(2, 300, 1024, device="cuda", generator=g).bfloat16()
     assert torch.equal(_residual(x, ls, y), x + ls(y))
+
+
+def test_gelu_matches_torch():
+    """Exact-erf GELU of bf16 values equals torch's bf16 F.gelu (same fp32
+    expression); at most a last-bit difference on a tiny fraction."""
+    from gpa_vggt_b200 import kernels
+    g = torch.Generator(device="cuda").manual_seed(4)
+    x = (torch.randn(3001, 4096, device="cuda", generator=g) * 3).bfloat16()
+    got, ref = kernels.gelu(x), F.gelu(x)
+    _ulp_ok(got, ref, frac=1e-3)
+
+
+def test_mlp_uses_fused_gelu_and_matches():
+    from gpa_vggt_b200.vggt.layers import Mlp
+    g = torch.Generator(device="cuda").manual_seed(5)
+    mlp = Mlp(256, 1024).cuda().bfloat16()
+    x = torch.randn(4, 77, 256, device="cuda", generator=g).bfloat16()
+    with torch.no_grad():
+        got = mlp(x)
+        ref = mlp.fc2(F.gelu(mlp.fc1(x)))
+    rel = float((got.float() - ref.float()).norm() / ref.float().norm())
+    assert rel < 1e-3, rel
