@@ -54,3 +54,33 @@ def test_argument_errors_are_reported_without_launching(lib):
     assert rc == 3
     with pytest.raises(_lib.GpaError):
         _lib.check(rc, "gpa_sim_argmax")
+
+
+def test_argument_errors_of_the_block_kernels(lib):
+    """The fused block/head kernels validate shapes and alignment before any
+    launch (a misaligned pointer never reaches a 16-byte vector access)."""
+    from gpa_vggt_b200 import _lib
+    lib = _lib.load()
+    odd = ctypes.c_void_p(8)      # not 16-byte aligned
+    ok = ctypes.c_void_p(256)
+    # GELU: element count must be a multiple of 8; buffers 16-byte aligned
+    assert lib.gpa_gelu_bf16(ok, 12, ok, None) == 3
+    assert b"multiple of 8" in lib.gpa_last_error()
+    assert lib.gpa_gelu_bf16(odd, 16, ok, None) == 1
+    assert lib.gpa_gelu_bf16(ok, 0, ok, None) == 0          # empty: nothing to do
+    # residual + LayerScale: cols % 8, aligned rows
+    assert lib.gpa_residual_scale_bf16(ok, 1024, ok, 1024, ok, 4, 1020, ok, 1024, None) == 3
+    assert lib.gpa_residual_scale_bf16(ok, 1021, ok, 1024, ok, 4, 1024, ok, 1024, None) == 1
+    # DPT resize: dtype, channels % 8, channels-last alignment
+    f32, bf16 = _lib.GPA_DTYPE_F32, _lib.GPA_DTYPE_BF16
+    assert lib.gpa_upsample_bilinear_bf16(ok, 7, 1, 8, 4, 4, 128, 32, 8, None, 0, 0, 0, 8, 8, ok,
+                                          512, 64, 8, None) == 1
+    assert lib.gpa_upsample_bilinear_bf16(ok, bf16, 1, 12, 4, 4, 192, 48, 12, None, 0, 0, 0, 8, 8, ok,
+                                          768, 96, 12, None) == 3
+    assert lib.gpa_upsample_bilinear_bf16(ok, f32, 1, 8, 4, 4, 130, 32, 8, None, 0, 0, 0, 8, 8, ok,
+                                          512, 64, 8, None) == 1
+    assert b"aligned" in lib.gpa_last_error()
+    # LSE combine: strides in multiples of 8 elements
+    A = _lib.i64array
+    assert lib.gpa_lse_combine(2, 2, 4, 64, ok, A([64, 512, 4]), ok, A([8, 4, 1]), ok, A([64, 512, 128]),
+                               ok, A([8, 4, 1]), ok, A([64, 512, 128]), None) == 1
