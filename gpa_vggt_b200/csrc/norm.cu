@@ -15,13 +15,23 @@
 namespace gpa {
 namespace norm {
 
-template <typename W>
-__device__ __forceinline__ float ldw(const W* p, int i);
-template <>
-__device__ __forceinline__ float ldw<float>(const float* p, int i) { return p[i]; }
-template <>
-__device__ __forceinline__ float ldw<__nv_bfloat16>(const __nv_bfloat16* p, int i) {
-  return __bfloat162float(p[i]);
+
+// 8 consecutive parameters (weight or bias) as floats, one or two vector loads.
+__device__ __forceinline__ void ldw8(const __nv_bfloat16* p, int i, float* v) {
+  const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p + i));
+  const __nv_bfloat162* e = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 f = __bfloat1622float2(e[k]);
+    v[2 * k] = f.x;
+    v[2 * k + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void ldw8(const float* p, int i, float* v) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p + i));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(p + i) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
 // One warp per row; cols % 256 == 0, cols <= 4096 (16-byte vectors per lane).
@@ -67,12 +77,15 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const __nv_bfloat16* __r
 #pragma unroll
   for (int u = 0; u < VPL; ++u) {
     const int c0 = (u * 32 + lane) * 8;
+    float wv[8], bv[8];
+    ldw8(w, c0, wv);
+    ldw8(b, c0, bv);
     uint4 raw;
     __nv_bfloat162* e = reinterpret_cast<__nv_bfloat162*>(&raw);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float y0 = fmaf((v[u][2 * i] - mean) * rstd, ldw(w, c0 + 2 * i), ldw(b, c0 + 2 * i));
-      const float y1 = fmaf((v[u][2 * i + 1] - mean) * rstd, ldw(w, c0 + 2 * i + 1), ldw(b, c0 + 2 * i + 1));
+      const float y0 = fmaf((v[u][2 * i] - mean) * rstd, wv[2 * i], bv[2 * i]);
+      const float y1 = fmaf((v[u][2 * i + 1] - mean) * rstd, wv[2 * i + 1], bv[2 * i + 1]);
       e[i] = __floats2bfloat162_rn(y0, y1);
     }
     reinterpret_cast<uint4*>(orow)[u * 32 + lane] = raw;
@@ -130,11 +143,11 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
   const float rstd = rsqrtf(q * (1.f / 64.f) + eps);
   const W* w = which ? kw : qw;
   const W* b = which ? kb : qb;
+  float wv[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f}, bv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (w) ldw8(w, sub * 8, wv);
+  if (b) ldw8(b, sub * 8, bv);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int f = sub * 8 + i;
-    v[i] = fmaf((v[i] - mean) * rstd, w ? ldw(w, f) : 1.f, b ? ldw(b, f) : 0.f);
-  }
+  for (int i = 0; i < 8; ++i) v[i] = fmaf((v[i] - mean) * rstd, wv[i], bv[i]);
   if (pos) {
     const int half = sub >> 2, within = (sub & 3) * 8;   // feature offset inside the half
     int p = (int)pos[tok * 2 + half];
@@ -231,7 +244,8 @@ extern "C" int gpa_layernorm_bf16(const void* x, int64_t x_stride, int rows, int
                                   void* out, int64_t out_stride, void* stream) {
   if (rows < 0 || cols <= 0 || cols % 256 || cols > 4096)
     return fail(GPA_ERR_UNSUPPORTED, "gpa_layernorm_bf16: cols must be a multiple of 256, <= 4096");
-  if (x_stride % 8 || out_stride % 8 || !aligned16(x) || !aligned16(out) || !weight || !bias)
+  if (x_stride % 8 || out_stride % 8 || !aligned16(x) || !aligned16(out) || !weight || !bias ||
+      !aligned16(weight) || !aligned16(bias))
     return fail(GPA_ERR_INVALID, "gpa_layernorm_bf16: 16-byte aligned rows and weight/bias required");
   if (param_dtype != GPA_DTYPE_F32 && param_dtype != GPA_DTYPE_BF16)
     return fail(GPA_ERR_INVALID, "gpa_layernorm_bf16: weight dtype must be f32 or bf16");
@@ -278,6 +292,9 @@ extern "C" int gpa_qk_norm_rope(const void* qkv, int64_t token_stride, int64_t q
     return fail(GPA_ERR_INVALID, "gpa_qk_norm_rope: rotary tables missing");
   if (positions && (!aligned16(cos_table) || !aligned16(sin_table)))
     return fail(GPA_ERR_INVALID, "gpa_qk_norm_rope: rotary tables must be 16-byte aligned");
+  if ((q_weight && !aligned16(q_weight)) || (q_bias && !aligned16(q_bias)) ||
+      (k_weight && !aligned16(k_weight)) || (k_bias && !aligned16(k_bias)))
+    return fail(GPA_ERR_INVALID, "gpa_qk_norm_rope: norm weights must be 16-byte aligned");
   if (param_dtype != GPA_DTYPE_F32 && param_dtype != GPA_DTYPE_BF16)
     return fail(GPA_ERR_INVALID, "gpa_qk_norm_rope: weight dtype must be f32 or bf16");
   const int64_t rows = 2ll * tokens * heads;
