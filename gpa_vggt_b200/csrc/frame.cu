@@ -154,8 +154,8 @@ __global__ void __launch_bounds__(256) pool_kernel(const __nv_bfloat16* __restri
   }
 }
 
-// One warp per row: o = bf16(bf16(oa*ca) + ob*cb) with ca, cb the normalised
-// partition weights rounded to bf16, as the reference's in-place mul_/addcmul_.
+// o = bf16(bf16(oa*ca) + ob*cb) with ca, cb the normalised partition weights
+// rounded to bf16, as the reference's in-place mul_/addcmul_.
 __global__ void __launch_bounds__(256) combine_kernel(
     int heads, int frames, int rows, const __nv_bfloat16* __restrict__ oa, int64_t a0, int64_t a1,
     int64_t a2, const float* __restrict__ la, int64_t la0, int64_t la1, int64_t la2,
