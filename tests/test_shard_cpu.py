@@ -109,3 +109,39 @@ def test_frame_sharded_forward_matches_unsharded(tmp_path):
         assert torch.allclose(got["tap"], want, atol=1e-4, rtol=1e-4), \
             float((got["tap"] - want).abs().max())
         assert torch.allclose(got["pose"], ref_pose, atol=1e-4, rtol=1e-4)
+
+
+def _gather_worker(rank, world, port, tmpdir):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from gpa_vggt_b200.vggt.shard import FrameShard
+    sh = FrameShard(4)
+    assert sh.kv_group is not None
+    k = torch.full((3, 2, 4), float(rank), dtype=torch.float32)
+    v = torch.full((3, 2, 4), 10.0 + rank, dtype=torch.bfloat16)
+    # one exchange of a stacked [N, 2, ...] buffer, and two exchanges of mixed dtypes,
+    # in flight together with a gather on the main communicator
+    kv, w1 = sh.gather_async(torch.stack((k, v.float()), 1))
+    kf, w2 = sh.gather_async(k)
+    vf, w3 = sh.gather_async(v)
+    small = sh.gather(torch.tensor([rank], dtype=torch.int64))
+    for w in (w1, w2, w3):
+        w.wait()
+    torch.save({"kv": kv, "k": kf, "v": vf, "small": small}, os.path.join(tmpdir, f"g{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_gather_async_on_the_kv_communicator(tmp_path):
+    world = 2
+    mp.start_processes(_gather_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       start_method="spawn")
+    for r in range(world):
+        got = torch.load(tmp_path / f"g{r}.pt")
+        assert got["small"].tolist() == [0, 1]
+        assert got["k"].shape == (6, 2, 4) and got["v"].dtype == torch.bfloat16
+        assert got["k"][:3].eq(0).all() and got["k"][3:].eq(1).all()
+        assert got["v"][:3].float().eq(10).all() and got["v"][3:].float().eq(11).all()
+        assert torch.equal(got["kv"][:, 0], got["k"]) and torch.equal(got["kv"][:, 1], got["v"].float())
