@@ -102,78 +102,82 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     const W* __restrict__ kw, const W* __restrict__ kb, float eps, const int64_t* __restrict__ pos,
     const float* __restrict__ cos_tab, const float* __restrict__ sin_tab, int n_pos,
     __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_out, int64_t out_tok_stride) {
-  // 8 lanes per 64-wide head row, 8 consecutive features per lane: 16-byte
-  // coalesced loads and stores, mean/variance by xor-shuffles inside the
-  // 8-lane group, the rotate-half partner (feature i +- 16) in lane ^ 2.
-  const int64_t per = (int64_t)tokens * heads;
-  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
-  if (row >= 2 * per) return;          // whole 8-lane groups leave together
+  // 8 lanes per (token, head), 8 consecutive features per lane, for both the
+  // q and the k row (they share the index math and the rotary table loads):
+  // 16-byte coalesced loads and stores, mean/variance by xor-shuffles inside
+  // the 8-lane group, the rotate-half partner (feature i +- 16) in lane ^ 2.
+  const uint32_t per = (uint32_t)tokens * (uint32_t)heads;   // the launcher bounds per * 8
+  const uint32_t row = (blockIdx.x * blockDim.x + threadIdx.x) >> 3;
+  if (row >= per) return;              // whole 8-lane groups leave together
   const int lane = threadIdx.x & 31, sub = lane & 7;
   const unsigned gmask = 0xffu << (lane & 24);
-  const int which = row >= per;        // 0 = q, 1 = k
-  const int64_t r = row - which * per;
-  const int64_t tok = r / heads;
-  const int hh = (int)(r - tok * heads);
-  const __nv_bfloat16* src = qkv + tok * tok_stride + (which ? k_off : q_off) + hh * 64 + sub * 8;
-  float v[8];
-  {
-    const uint4 raw = *reinterpret_cast<const uint4*>(src);  // may be rewritten in place: no nc path
-    const __nv_bfloat162* e = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = __bfloat1622float2(e[i]);
-      v[2 * i] = f.x;
-      v[2 * i + 1] = f.y;
-    }
-  }
-  float s = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
-  s += __shfl_xor_sync(gmask, s, 1);
-  s += __shfl_xor_sync(gmask, s, 2);
-  s += __shfl_xor_sync(gmask, s, 4);
-  const float mean = s * (1.f / 64.f);
-  float q = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float d = v[i] - mean;
-    q = fmaf(d, d, q);
-  }
-  q += __shfl_xor_sync(gmask, q, 1);
-  q += __shfl_xor_sync(gmask, q, 2);
-  q += __shfl_xor_sync(gmask, q, 4);
-  const float rstd = rsqrtf(q * (1.f / 64.f) + eps);
-  const W* w = which ? kw : qw;
-  const W* b = which ? kb : qb;
-  float wv[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f}, bv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  if (w) ldw8(w, sub * 8, wv);
-  if (b) ldw8(b, sub * 8, bv);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = fmaf((v[i] - mean) * rstd, wv[i], bv[i]);
+  const uint32_t tok = row / (uint32_t)heads;
+  const int hh = (int)(row - tok * (uint32_t)heads);
+  const int64_t tok64 = tok;
+  float c[8], sn[8];
+  const bool lower = (sub & 3) < 2;     // features 0..15 of a half pair with +16, 16..31 with -16
   if (pos) {
     const int half = sub >> 2, within = (sub & 3) * 8;   // feature offset inside the half
-    int p = (int)pos[tok * 2 + half];
+    int p = (int)pos[tok64 * 2 + half];
     p = min(max(p, 0), n_pos - 1);
     const float4* c4 = reinterpret_cast<const float4*>(cos_tab + (int64_t)p * 32 + within);
     const float4* s4 = reinterpret_cast<const float4*>(sin_tab + (int64_t)p * 32 + within);
     const float4 ca = __ldg(c4), cb = __ldg(c4 + 1), sa = __ldg(s4), sb = __ldg(s4 + 1);
-    const float c[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
-    const float sn[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
-    const bool lower = within < 16;   // features 0..15 pair with +16, 16..31 with -16
-    float o[8];
+    c[0] = ca.x; c[1] = ca.y; c[2] = ca.z; c[3] = ca.w; c[4] = cb.x; c[5] = cb.y; c[6] = cb.z; c[7] = cb.w;
+    sn[0] = sa.x; sn[1] = sa.y; sn[2] = sa.z; sn[3] = sa.w; sn[4] = sb.x; sn[5] = sb.y; sn[6] = sb.z; sn[7] = sb.w;
+  }
+  auto one = [&](int64_t off, const W* w, const W* b, __nv_bfloat16* dst) {
+    const __nv_bfloat16* src = qkv + tok64 * tok_stride + off + hh * 64 + sub * 8;
+    float v[8];
+    {
+      const uint4 raw = *reinterpret_cast<const uint4*>(src);  // may be rewritten in place: no nc path
+      const __nv_bfloat162* e = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(e[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+      }
+    }
+    float s = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+    s += __shfl_xor_sync(gmask, s, 1);
+    s += __shfl_xor_sync(gmask, s, 2);
+    s += __shfl_xor_sync(gmask, s, 4);
+    const float mean = s * (1.f / 64.f);
+    float q = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float partner = __shfl_xor_sync(gmask, v[i], 2);
-      // separate roundings of the two products and the sum, as t*cos + rot(t)*sin
-      o[i] = __fadd_rn(__fmul_rn(v[i], c[i]), __fmul_rn(lower ? -partner : partner, sn[i]));
+      const float d = v[i] - mean;
+      q = fmaf(d, d, q);
     }
+    q += __shfl_xor_sync(gmask, q, 1);
+    q += __shfl_xor_sync(gmask, q, 2);
+    q += __shfl_xor_sync(gmask, q, 4);
+    const float rstd = rsqrtf(q * (1.f / 64.f) + eps);
+    float wv[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f}, bv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (w) ldw8(w, sub * 8, wv);
+    if (b) ldw8(b, sub * 8, bv);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = o[i];
-  }
-  __nv_bfloat16* dst = (which ? k_out : q_out) + tok * out_tok_stride + hh * 64 + sub * 8;
-  uint4 raw;
-  __nv_bfloat162* e = reinterpret_cast<__nv_bfloat162*>(&raw);
+    for (int i = 0; i < 8; ++i) v[i] = fmaf((v[i] - mean) * rstd, wv[i], bv[i]);
+    if (pos) {
+      float o[8];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) e[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-  *reinterpret_cast<uint4*>(dst) = raw;
+      for (int i = 0; i < 8; ++i) {
+        const float partner = __shfl_xor_sync(gmask, v[i], 2);
+        // separate roundings of the two products and the sum, as t*cos + rot(t)*sin
+        o[i] = __fadd_rn(__fmul_rn(v[i], c[i]), __fmul_rn(lower ? -partner : partner, sn[i]));
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = o[i];
+    }
+    uint4 raw;
+    __nv_bfloat162* e = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) e[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4*>(dst + tok64 * out_tok_stride + hh * 64 + sub * 8) = raw;
+  };
+  one(q_off, qw, qb, q_out);
+  one(k_off, kw, kb, k_out);
 }
 
 }  // namespace norm
@@ -297,9 +301,10 @@ extern "C" int gpa_qk_norm_rope(const void* qkv, int64_t token_stride, int64_t q
     return fail(GPA_ERR_INVALID, "gpa_qk_norm_rope: norm weights must be 16-byte aligned");
   if (param_dtype != GPA_DTYPE_F32 && param_dtype != GPA_DTYPE_BF16)
     return fail(GPA_ERR_INVALID, "gpa_qk_norm_rope: weight dtype must be f32 or bf16");
-  const int64_t rows = 2ll * tokens * heads;
-  if (rows == 0) return ok();
-  const unsigned blocks = (unsigned)((rows * 8 + 255) / 256);   // 8 lanes per row
+  const int64_t per = (int64_t)tokens * heads;
+  if (per == 0) return ok();
+  if (per * 8 >= (1ll << 32)) return fail(GPA_ERR_UNSUPPORTED, "gpa_qk_norm_rope: too many rows");
+  const unsigned blocks = (unsigned)((per * 8 + 255) / 256);   // 8 lanes per (token, head)
   cudaStream_t st = (cudaStream_t)stream;
   if (param_dtype == GPA_DTYPE_BF16)
     norm::qk_norm_rope_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
