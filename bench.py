@@ -22,8 +22,10 @@ sharded by query frame (gpa_vggt_b200/vggt/shard.py): each rank runs S/N
 frames end to end and the global blocks all-gather what their keys need
 (strong scaling; the time is the max over ranks).  The merged_block workload
 runs one replica per rank (weak scaling).  --impl reference times the
-reference's CPU path (the oracle port in oracle/, torch on all host cores) on
-a bounded sample and extrapolates it to the same workload.
+reference's own CPU path on all host cores (oracle/reference_runs.py, with the
+unmodified reference from baseline/_ref; the port in oracle/ where it is
+missing): the whole fp32 forward at S <= 10, and at S=200 its pieces on
+bounded samples composed by the block schedule (an extrapolation, labelled).
 """
 from __future__ import annotations
 
@@ -179,101 +181,27 @@ def merged_block(x, qkv, ratio, out=None):
 
 
 # ----------------------------------------------------------------------------
-# CPU baseline: the reference path on the host cores, composed from samples
+# CPU baseline: the reference's own CPU path on the host cores
 # ----------------------------------------------------------------------------
-def _t(fn, reps=1):
-    t0 = time.perf_counter()
-    for _ in range(reps):
-        fn()
-    return (time.perf_counter() - t0) / reps
-
-
-def merged_len(S, ratio):
-    nd = P_TOK + (S - 1) * 329
-    ns = S * P_TOK - nd
-    r = int(S * P_TOK * ratio)
-    return nd if r >= ns else ns - r + nd
-
-
-def cpu_block_parts(S):
-    """Seconds on the host cores (torch CPU fp32, all threads) for the pieces of
-    one GPA forward at S frames, each measured on a bounded sample and scaled by
-    the fraction of rows / frames it covers."""
+def cpu_reference(S, vanilla=False, reps=1):
+    """(ms per forward, kind, sample note, extrapolated) of the reference's CPU
+    forward at S frames (oracle/reference_runs.py): the reference's own modules
+    from baseline/_ref when installed (kind "reference"), else the port.  At
+    S <= 10 the whole forward runs; above, its pieces are timed on bounded
+    samples and composed by the block schedule."""
     import torch
-    import torch.nn.functional as F
-    from oracle import gpa_oracle as O
+    from oracle import reference_runs as RR
     torch.set_num_threads(os.cpu_count() or 1)
-    g = torch.Generator().manual_seed(0)
-    N = S * P_TOK
-    parts = {}
-    # linear layers of one block (qkv, proj, fc1, fc2) on 1024 rows
-    R = 1024
-    xr = torch.randn(R, 1024, generator=g)
-    w = [torch.randn(o, i, generator=g) * 0.02 for o, i in ((3072, 1024), (1024, 1024), (4096, 1024), (1024, 4096))]
-    def lin():
-        F.linear(xr, w[0]); F.linear(xr, w[1]); h = F.linear(xr, w[2]); F.linear(h, w[3])
-    parts["linear_per_block"] = _t(lin, 2) * N / R
-    # per-frame attention (frame blocks, DINO blocks, own-frame part of early blocks)
-    qf = torch.randn(1, 16, P_TOK, 64, generator=g)
-    parts["frame_attn_per_block"] = _t(lambda: F.scaled_dot_product_attention(qf, qf, qf), 2) * S
-    # shared-set attention of an early block on a query sample
-    qs = 2048
-    q = torch.randn(1, 16, qs, 64, generator=g)
-    ksh = torch.randn(1, 16, 30 * S, 64, generator=g)
-    parts["shared_attn_per_block"] = _t(lambda: F.scaled_dot_product_attention(q, ksh, ksh,
-                                        attn_mask=torch.zeros(1, 1, 1, 30 * S)), 1) * N / qs
-    # merged-block matching (roles, projection, normalise) at full size, similarity on a sample
-    x = torch.randn(N, 1024, generator=g)
-    def match():
-        rand = torch.randint(4, (S - 1, 18, 18), generator=g)
-        mask = O.dst_mask(S, 37, 37, 2, 2, 5, rand)
-        d, s_ = O.split_positions(mask)
-        mn = O.normalize_rows(x @ torch.randn(1024, 128, generator=g))
-        return mn, d, s_
-    t0 = time.perf_counter()
-    mn, dst, src = match()
-    t_match = time.perf_counter() - t0
-    sub = max(256, src.numel() // 256)
-    t_sim = _t(lambda: (mn[src[:sub]] @ mn[dst].T).max(dim=1)) * src.numel() / sub
-    kv = torch.randn(N, 1024, generator=g)
-    idx = torch.randint(0, dst.numel(), (src.numel(),), generator=g)
-    def merge():
-        for _ in range(2):
-            mid = kv[dst].clone()
-            mid.index_add_(0, idx, kv[src])
-    t_merge = _t(merge)
-    for name, ratio in (("merged_0.98", 0.98), ("merged_0.2", 0.2)):
-        nm_ = merged_len(S, ratio)
-        qq = torch.randn(1, 16, 512, 64, generator=g)
-        kk = torch.randn(1, 16, nm_, 64, generator=g)
-        b = torch.rand(1, 1, 1, nm_, generator=g)
-        t_att = _t(lambda: F.scaled_dot_product_attention(qq, kk, kk, attn_mask=b)) * N / 512
-        parts[f"{name}_per_block"] = t_match + t_sim + t_merge + t_att
-    return parts
-
-
-def cpu_forward_ms(S, vanilla=False):
-    p = cpu_block_parts(S)
-    lin = p["linear_per_block"] * 72                      # 24 DINO + 24 frame + 24 global
-    frame = p["frame_attn_per_block"] * (24 + 24)         # DINO + frame blocks
-    if vanilla:
-        glob = merged_ms = 0.0
-        import torch
-        import torch.nn.functional as F
-        N = S * P_TOK
-        q = torch.randn(1, 16, 512, 64)
-        k = torch.randn(1, 16, N, 64)
-        glob = _t(lambda: F.scaled_dot_product_attention(q, k, k)) * N / 512 * 24
-    else:
-        glob = (9 * (p["frame_attn_per_block"] + p["shared_attn_per_block"])
-                + 11 * p["merged_0.98_per_block"] + 4 * p["merged_0.2_per_block"])
-    total = lin + frame + glob
-    sample = (f"GPA forward at S={S} composed from sampled components on the host cores "
-              f"(torch CPU fp32): linears on 1024 rows, per-frame attention on 1 frame, "
-              f"global/merged attention on 512-2048 query rows, similarity on 1/256 of the src "
-              f"rows, matching and K/V merge at full size; scaled by rows/frames and the block "
-              f"schedule (24 DINO + 24 frame + 9 early + 11 merged + 4 core); heads excluded")
-    return total * 1e3, sample
+    if not RR.have_reference():
+        return RR.port_forward_ms(S, vanilla), "port", RR.port_sample_note(S, vanilla), True
+    if S <= 10:
+        model = RR.build_cpu_model(vanilla)
+        ms = statistics.median(RR.forward_ms(model, S) for _ in range(reps))
+        return ms, "reference", (f"the reference's whole fp32 forward at S={S} (baseline/_ref, "
+                                 f"aggregator + camera + DPT heads)"), False
+    comp = RR.Composer(S, vanilla)
+    ms = statistics.median(comp.compose_ms(comp.parts(reps=1)) for _ in range(reps))
+    return ms, "reference", RR.composed_sample_note(S, vanilla), True
 
 
 # ----------------------------------------------------------------------------
@@ -313,24 +241,54 @@ def main():
             "config": config}
 
     if args.impl == "reference":
+        # the reference's CPU path on the host cores (rank 0 only); a step is
+        # one run of the reference's forward at S <= 10, else one bounded sample
+        # of every piece of the S=200 forward, composed into its time
         if rank != 0:
             return
-        vals, sample = [], ""
-        for _ in range(max(1, args.warmup) + args.steps):
-            if fwd:
-                ms, sample = cpu_forward_ms(S, args.vanilla)
-            else:
-                p = cpu_block_parts(S)
-                ms = p["merged_0.98_per_block"] * 1e3
-                sample = f"one merged block at S={S}, composed from sampled components"
-            vals.append(ms)
-        ms = statistics.mean(vals[-args.steps:])
-        line = dict(base, impl="reference", value=ms, ms_per_step=ms,
-                    cpu_baseline={"value": ms, "unit": "ms", "cores": os.cpu_count(), "kind": "port",
+        import torch
+        from oracle import reference_runs as RR
+        torch.set_num_threads(os.cpu_count() or 1)
+        if not fwd:
+            print(json.dumps(dict(base, impl="reference", unavailable=(
+                "the merged_block workload has no reference arm; use --workload forward"))), flush=True)
+            return
+        have = RR.have_reference()
+        kind = "reference" if have else "port"
+        direct = have and S <= 10
+        if direct:
+            model = RR.build_cpu_model(args.vanilla)
+            one = lambda: RR.forward_ms(model, S)  # noqa: E731
+            sample = f"the reference's whole fp32 forward at S={S} (baseline/_ref)"
+        elif have:
+            comp = RR.Composer(S, args.vanilla)
+            one = lambda: comp.compose_ms(comp.parts(reps=1))  # noqa: E731
+            sample = RR.composed_sample_note(S, args.vanilla)
+        else:
+            one = lambda: RR.port_forward_ms(S, args.vanilla)  # noqa: E731
+            sample = RR.port_sample_note(S, args.vanilla)
+        for _ in range(args.warmup):
+            one()
+        vals, walls = [], []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            vals.append(one())
+            walls.append((time.perf_counter() - t0) * 1e3)
+        ms = statistics.median(vals)
+        step_ms = statistics.mean(walls)
+        spread = (max(vals) - min(vals)) / ms if ms else 0.0
+        cores = torch.get_num_threads()
+        line = dict(base, impl="reference", value=ms, ms_per_step=step_ms, dtype="fp32",
+                    extrapolated=not direct,
+                    step=("one whole forward" if direct else
+                          "one bounded sample of every piece of the forward, timed and composed "
+                          "into value (ms_per_step is the sample's own wall time)"),
+                    steps_values_ms={"median": ms, "min": min(vals), "max": max(vals),
+                                     "spread": spread},
+                    cpu_baseline={"value": ms, "unit": "ms", "cores": cores, "kind": kind,
                                   "sample": sample},
                     e2e={"value": ms, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
-        if fwd:
-            line["frames_per_s"] = S / (ms / 1e3)
+        line["frames_per_s"] = S / (ms / 1e3)
         print(json.dumps(line), flush=True)
         return
 
@@ -469,13 +427,10 @@ def main():
     if fwd:
         line["frames_per_s"] = S / (ms / 1e3)
         line["gpu_memory_peak_gib"] = torch.cuda.max_memory_allocated(dev) / 2 ** 30
-    if world == 1 and not args.no_cpu:   # the CPU baseline is an N=1 figure
-        if fwd:
-            cms, sample = cpu_forward_ms(S, args.vanilla)
-        else:
-            cms, sample = cpu_block_parts(S)["merged_0.98_per_block"] * 1e3, f"merged block at S={S}"
-        line["cpu_baseline"] = {"value": cms, "unit": "ms", "cores": os.cpu_count(), "kind": "port",
-                                "sample": sample}
+    if world == 1 and not args.no_cpu and fwd:   # the CPU baseline is an N=1 figure
+        cms, kind, sample, extra = cpu_reference(S, args.vanilla)
+        line["cpu_baseline"] = {"value": cms, "unit": "ms", "cores": torch.get_num_threads(),
+                                "kind": kind, "sample": sample, "extrapolated": extra}
     if world > 1:
         torch.distributed.destroy_process_group()
     if rank == 0:

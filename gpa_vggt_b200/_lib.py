@@ -31,6 +31,7 @@ SIGNATURES = {
     "gpa_version": (_c_int, []),
     "gpa_last_error": (ctypes.c_char_p, []),
     "gpa_launch_count": (_c_i64, []),
+    "gpa_wait_selftest": (_c_int, [ctypes.c_uint64, _vp, _vp]),
     "gpa_sim_argmax": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_i64, _c_i64, _c_i64,
                                 _c_i64, _vp, _vp, _vp, _vp]),
     "gpa_merge_counts": (_c_int, [_c_int] * 7 + [ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
@@ -45,6 +46,11 @@ SIGNATURES = {
                                        _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                                        _c_i64, _c_i64, _c_i64, _c_f32, _vp, _c_i64, _c_i64, _c_i64,
                                        _vp, _c_i64, _c_i64, _vp, _vp]),
+    "gpa_attention_keybias_combine": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                               _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+                                               _c_i64, _c_i64, _c_i64, _c_i64, _c_f32, _vp, _c_i64, _c_i64,
+                                               _c_i64, _vp, _c_i64, _c_i64, _vp, _c_i64, _c_i64, _c_i64,
+                                               _vp, _c_i64, _c_i64, _vp, _vp]),
     "gpa_layernorm_bf16": (_c_int, [_vp, _c_i64, _c_int, _c_int, _vp, _vp, _c_int, _c_f32, _vp, _c_i64, _vp]),
     "gpa_upsample_bilinear_bf16": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_i64, _c_i64,
                                             _c_i64, _vp, _c_i64, _c_i64, _c_int, _c_int, _c_int, _vp,

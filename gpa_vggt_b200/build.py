@@ -13,12 +13,14 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libgpa_b200.so"
+OBJ = PKG / "_build"
 HEADER = ROOT / "include" / "gpa_b200.h"
 
 SOURCES = ["merge.cu", "sim_argmax.cu", "attention.cu", "frame.cu", "norm.cu", "dpt.cu"]
@@ -46,18 +48,28 @@ def _stale() -> bool:
     return any(d.stat().st_mtime > t for d in deps)
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    """Compile every CUDA source into one shared library (in-tree)."""
-    if not force and not _stale():
-        return LIB
-    nvcc = _nvcc()
-    tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc, *NVCC_FLAGS, "-shared", "-o", str(tmp), *[str(CSRC / s) for s in SOURCES]]
+def _run(cmd, verbose):
     if verbose:
         print(" ".join(cmd), flush=True)
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
+        raise RuntimeError(f"nvcc failed ({r.returncode}):\n{' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    """Compile every CUDA source (one nvcc per file, in parallel) and link
+    them into one shared library (in-tree)."""
+    if not force and not _stale():
+        return LIB
+    nvcc = _nvcc()
+    OBJ.mkdir(exist_ok=True)
+    objs = [OBJ / (Path(s).stem + ".o") for s in SOURCES]
+    jobs = [[nvcc, *NVCC_FLAGS, "-c", "-o", str(o), str(CSRC / s)] for s, o in zip(SOURCES, objs)]
+    with ThreadPoolExecutor(max_workers=min(len(jobs), os.cpu_count() or 1)) as ex:
+        list(ex.map(lambda c: _run(c, verbose), jobs))
+    tmp = LIB.with_suffix(".so.tmp")
+    _run([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", str(tmp),
+          *[str(o) for o in objs]], verbose)
     os.replace(tmp, LIB)
     return LIB
 

@@ -98,6 +98,13 @@ struct Params {
   int64_t o_sb, o_sh, o_sm;
   float* lse;
   int64_t lse_sb, lse_sh;
+  // optional second partition of the same softmax, combined in the epilogue
+  // (vggt/layers/attention.py:164-176): its normalised output rows and log2
+  // row sums; the output may alias comb_o (each row is read before written)
+  const __nv_bfloat16* comb_o;
+  int64_t comb_sb, comb_sh, comb_sm;
+  const float* comb_lse;
+  int64_t comb_lse_sb, comb_lse_sh;
   int* status;
 };
 
@@ -425,19 +432,48 @@ __global__ void __launch_bounds__(THREADS, 1)
       tmem_wait_ld();
       const int row = q0 + t * BM + r;
       if (row < p.m && !*abort_flag) {
-        const float inv = 1.0f / l;
+        float lse_row = m_raw * p.scale_log2 + __log2f(l);
+        float cb = 1.0f / l;   // weight of this partition's unnormalised O
         __nv_bfloat16* orow = p.o + (int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)row * p.o_sm;
+        if (p.comb_o) {
+          // exact two-partition softmax: o = (wa*oa + wb*ob) / (wa + wb) with
+          // wa = 2^(lse_a - mx), wb = 2^(lse_b - mx), ob = O / l
+          const float la = p.comb_lse[(int64_t)b * p.comb_lse_sb + (int64_t)h * p.comb_lse_sh + row];
+          const float mx = fmaxf(la, lse_row);
+          const float wa = exp2f(la - mx), wb = exp2f(lse_row - mx);
+          const float inv = 1.0f / (wa + wb);
+          const float ca = wa * inv;
+          cb = wb * inv * cb;
+          lse_row = mx + __log2f(wa + wb);
+          const uint4* arow = reinterpret_cast<const uint4*>(
+              p.comb_o + (int64_t)b * p.comb_sb + (int64_t)h * p.comb_sh + (int64_t)row * p.comb_sm);
+          uint4 oa[HD / 8];
 #pragma unroll
-        for (int u = 0; u < HD / 8; ++u) {
-          uint4 pk;
-          pk.x = pack_bf16x2(__uint_as_float(ov[8 * u + 0]) * inv, __uint_as_float(ov[8 * u + 1]) * inv);
-          pk.y = pack_bf16x2(__uint_as_float(ov[8 * u + 2]) * inv, __uint_as_float(ov[8 * u + 3]) * inv);
-          pk.z = pack_bf16x2(__uint_as_float(ov[8 * u + 4]) * inv, __uint_as_float(ov[8 * u + 5]) * inv);
-          pk.w = pack_bf16x2(__uint_as_float(ov[8 * u + 6]) * inv, __uint_as_float(ov[8 * u + 7]) * inv);
-          reinterpret_cast<uint4*>(orow)[u] = pk;
+          for (int u = 0; u < HD / 8; ++u) oa[u] = arow[u];   // the whole row before any store
+#pragma unroll
+          for (int u = 0; u < HD / 8; ++u) {
+            const __nv_bfloat162* e = reinterpret_cast<const __nv_bfloat162*>(&oa[u]);
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float2 f = __bfloat1622float2(e[i]);
+              w[i] = pack_bf16x2(fmaf(cb, __uint_as_float(ov[8 * u + 2 * i]), ca * f.x),
+                                 fmaf(cb, __uint_as_float(ov[8 * u + 2 * i + 1]), ca * f.y));
+            }
+            reinterpret_cast<uint4*>(orow)[u] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        } else {
+#pragma unroll
+          for (int u = 0; u < HD / 8; ++u) {
+            uint4 pk;
+            pk.x = pack_bf16x2(__uint_as_float(ov[8 * u + 0]) * cb, __uint_as_float(ov[8 * u + 1]) * cb);
+            pk.y = pack_bf16x2(__uint_as_float(ov[8 * u + 2]) * cb, __uint_as_float(ov[8 * u + 3]) * cb);
+            pk.z = pack_bf16x2(__uint_as_float(ov[8 * u + 4]) * cb, __uint_as_float(ov[8 * u + 5]) * cb);
+            pk.w = pack_bf16x2(__uint_as_float(ov[8 * u + 6]) * cb, __uint_as_float(ov[8 * u + 7]) * cb);
+            reinterpret_cast<uint4*>(orow)[u] = pk;
+          }
         }
-        if (p.lse)
-          p.lse[(int64_t)b * p.lse_sb + (int64_t)h * p.lse_sh + row] = m_raw * p.scale_log2 + __log2f(l);
+        if (p.lse) p.lse[(int64_t)b * p.lse_sb + (int64_t)h * p.lse_sh + row] = lse_row;
       }
     }
   }
@@ -485,32 +521,34 @@ static int check_regs() {
 }  // namespace attn
 }  // namespace gpa
 
-extern "C" int gpa_attention_keybias(const void* q, const void* k, const void* v, const float* bias,
-                                     int batch, int heads, int m, int n, int head_dim, int64_t q_sb,
-                                     int64_t q_sh, int64_t q_sm, int64_t k_sb, int64_t k_sh,
-                                     int64_t k_sn, int64_t v_sb, int64_t v_sh, int64_t v_sn,
-                                     int64_t bias_sb, int64_t bias_sh, float sm_scale, void* o,
-                                     int64_t o_sb, int64_t o_sh, int64_t o_sm, float* lse,
-                                     int64_t lse_sb, int64_t lse_sh, int* status, void* stream) {
-  using namespace gpa;
-  using namespace gpa::attn;
-  if (head_dim != HD) return fail(GPA_ERR_UNSUPPORTED, "gpa_attention_keybias: head_dim must be 64");
-  if (batch <= 0 || heads <= 0 || m < 0 || n <= 0)
-    return fail(GPA_ERR_INVALID, "gpa_attention_keybias: bad sizes");
-  if (!q || !k || !v || !o) return fail(GPA_ERR_INVALID, "gpa_attention_keybias: null pointer");
+namespace gpa {
+namespace attn {
+static int launch(const char* what, const void* q, const void* k, const void* v, const float* bias,
+                  int batch, int heads, int m, int n, int head_dim, int64_t q_sb, int64_t q_sh,
+                  int64_t q_sm, int64_t k_sb, int64_t k_sh, int64_t k_sn, int64_t v_sb, int64_t v_sh,
+                  int64_t v_sn, int64_t bias_sb, int64_t bias_sh, float sm_scale, void* o, int64_t o_sb,
+                  int64_t o_sh, int64_t o_sm, float* lse, int64_t lse_sb, int64_t lse_sh,
+                  const void* comb_o, int64_t comb_sb, int64_t comb_sh, int64_t comb_sm,
+                  const float* comb_lse, int64_t comb_lse_sb, int64_t comb_lse_sh, int* status,
+                  void* stream) {
+  if (head_dim != HD) return fail(GPA_ERR_UNSUPPORTED, "%s: head_dim must be 64", what);
+  if (batch <= 0 || heads <= 0 || m < 0 || n <= 0) return fail(GPA_ERR_INVALID, "%s: bad sizes", what);
+  if (!q || !k || !v || !o) return fail(GPA_ERR_INVALID, "%s: null pointer", what);
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
-    return fail(GPA_ERR_INVALID, "gpa_attention_keybias: q/k/v/o must be 16-byte aligned");
+    return fail(GPA_ERR_INVALID, "%s: q/k/v/o must be 16-byte aligned", what);
   if (o_sm % 8 || o_sh % 8 || o_sb % 8)
-    return fail(GPA_ERR_INVALID, "gpa_attention_keybias: o strides must be multiples of 8");
+    return fail(GPA_ERR_INVALID, "%s: o strides must be multiples of 8", what);
+  if (comb_o && (!comb_lse || !aligned16(comb_o) || comb_sm % 8 || comb_sh % 8 || comb_sb % 8))
+    return fail(GPA_ERR_INVALID, "%s: combine rows need their lse, 16-byte alignment and strides "
+                "that are multiples of 8", what);
   if (m == 0) return ok();
-  if ((int64_t)batch * heads > 65535)
-    return fail(GPA_ERR_UNSUPPORTED, "gpa_attention_keybias: batch*heads > 65535");
+  if ((int64_t)batch * heads > 65535) return fail(GPA_ERR_UNSUPPORTED, "%s: batch*heads > 65535", what);
   int rc = check_regs();
   if (rc) return rc;
   CUtensorMap mq, mk, mv;
-  rc = make_map4(&mq, q, m, heads, batch, q_sm, q_sh, q_sb, "gpa_attention_keybias(q)");
-  if (!rc) rc = make_map4(&mk, k, n, heads, batch, k_sn, k_sh, k_sb, "gpa_attention_keybias(k)");
-  if (!rc) rc = make_map4(&mv, v, n, heads, batch, v_sn, v_sh, v_sb, "gpa_attention_keybias(v)");
+  rc = make_map4(&mq, q, m, heads, batch, q_sm, q_sh, q_sb, what);
+  if (!rc) rc = make_map4(&mk, k, n, heads, batch, k_sn, k_sh, k_sb, what);
+  if (!rc) rc = make_map4(&mv, v, n, heads, batch, v_sn, v_sh, v_sb, what);
   if (rc) return rc;
   Params p;
   p.m = m; p.n = n; p.heads = heads;
@@ -519,9 +557,40 @@ extern "C" int gpa_attention_keybias(const void* q, const void* k, const void* v
   p.bias = bias; p.bias_sb = bias_sb; p.bias_sh = bias_sh;
   p.o = (__nv_bfloat16*)o; p.o_sb = o_sb; p.o_sh = o_sh; p.o_sm = o_sm;
   p.lse = lse; p.lse_sb = lse_sb; p.lse_sh = lse_sh;
+  p.comb_o = (const __nv_bfloat16*)comb_o; p.comb_sb = comb_sb; p.comb_sh = comb_sh; p.comb_sm = comb_sm;
+  p.comb_lse = comb_o ? comb_lse : nullptr; p.comb_lse_sb = comb_lse_sb; p.comb_lse_sh = comb_lse_sh;
   p.status = status;
   cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem::ALLOC);
   dim3 grid((m + 2 * BM - 1) / (2 * BM), batch * heads);
   attn_kernel<<<grid, THREADS, Smem::ALLOC, (cudaStream_t)stream>>>(mq, mk, mv, p);
-  return check_launch("gpa_attention_keybias");
+  return check_launch(what);
+}
+}  // namespace attn
+}  // namespace gpa
+
+extern "C" int gpa_attention_keybias(const void* q, const void* k, const void* v, const float* bias,
+                                     int batch, int heads, int m, int n, int head_dim, int64_t q_sb,
+                                     int64_t q_sh, int64_t q_sm, int64_t k_sb, int64_t k_sh,
+                                     int64_t k_sn, int64_t v_sb, int64_t v_sh, int64_t v_sn,
+                                     int64_t bias_sb, int64_t bias_sh, float sm_scale, void* o,
+                                     int64_t o_sb, int64_t o_sh, int64_t o_sm, float* lse,
+                                     int64_t lse_sb, int64_t lse_sh, int* status, void* stream) {
+  return gpa::attn::launch("gpa_attention_keybias", q, k, v, bias, batch, heads, m, n, head_dim, q_sb,
+                           q_sh, q_sm, k_sb, k_sh, k_sn, v_sb, v_sh, v_sn, bias_sb, bias_sh, sm_scale, o,
+                           o_sb, o_sh, o_sm, lse, lse_sb, lse_sh, nullptr, 0, 0, 0, nullptr, 0, 0,
+                           status, stream);
+}
+
+extern "C" int gpa_attention_keybias_combine(
+    const void* q, const void* k, const void* v, const float* bias, int batch, int heads, int m, int n,
+    int head_dim, int64_t q_sb, int64_t q_sh, int64_t q_sm, int64_t k_sb, int64_t k_sh, int64_t k_sn,
+    int64_t v_sb, int64_t v_sh, int64_t v_sn, int64_t bias_sb, int64_t bias_sh, float sm_scale,
+    const void* oa, int64_t oa_sb, int64_t oa_sh, int64_t oa_sm, const float* lse_a, int64_t lse_a_sb,
+    int64_t lse_a_sh, void* o, int64_t o_sb, int64_t o_sh, int64_t o_sm, float* lse, int64_t lse_sb,
+    int64_t lse_sh, int* status, void* stream) {
+  if (!oa || !lse_a) return gpa::fail(GPA_ERR_INVALID, "gpa_attention_keybias_combine: null partition");
+  return gpa::attn::launch("gpa_attention_keybias_combine", q, k, v, bias, batch, heads, m, n,
+                           head_dim, q_sb, q_sh, q_sm, k_sb, k_sh, k_sn, v_sb, v_sh, v_sn, bias_sb,
+                           bias_sh, sm_scale, o, o_sb, o_sh, o_sm, lse, lse_sb, lse_sh, oa, oa_sb,
+                           oa_sh, oa_sm, lse_a, lse_a_sb, lse_a_sh, status, stream);
 }

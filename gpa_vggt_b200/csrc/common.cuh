@@ -75,14 +75,15 @@ __device__ __forceinline__ bool bar_try_wait(uint64_t* bar, uint32_t parity) {
 // (time limit, or another thread of the CTA already aborted); the first thread
 // to time out records `code` in *status and raises *abort.
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                         int* status, int code) {
+                                         int* status, int code,
+                                         unsigned long long limit_ns = kWaitLimitNs) {
   if (bar_try_wait(bar, parity)) return true;
   unsigned long long t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
     if (bar_try_wait(bar, parity)) return true;
     if ((it & 63u) == 0) {
       if (*abort) return false;
-      if (global_ns() - t0 > kWaitLimitNs) {
+      if (global_ns() - t0 > limit_ns) {
         *abort = 1;
         if (status) atomicExch(status, code);
         return false;

@@ -247,6 +247,35 @@ extern "C" int gpa_lse_combine(int heads, int frames, int rows_per_frame, int he
   return check_launch("gpa_lse_combine");
 }
 
+// ---------------------------------------------------------------------------
+// failure-path self-test: one warp waits on an mbarrier that nothing arrives
+// on, through the same bounded wait the pipelined kernels use; the wait gives
+// up after limit_ns, records kDevTimeout in *status and the kernel returns.
+// Nothing else is in flight, so the context stays usable.
+// ---------------------------------------------------------------------------
+namespace gpa {
+__global__ void wait_selftest_kernel(unsigned long long limit_ns, int* status) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    bar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  wait_bar(&bar, 0, &abort_flag, status, kDevTimeout, limit_ns);
+  __syncthreads();
+}
+}  // namespace gpa
+
+extern "C" int gpa_wait_selftest(uint64_t limit_ns, int* status, void* stream) {
+  if (!status) return gpa::fail(GPA_ERR_INVALID, "gpa_wait_selftest: null status word");
+  if (limit_ns < 1000 || limit_ns > 10000000000ull)
+    return gpa::fail(GPA_ERR_INVALID, "gpa_wait_selftest: limit must be 1 us .. 10 s");
+  gpa::wait_selftest_kernel<<<1, 32, 0, (cudaStream_t)stream>>>((unsigned long long)limit_ns, status);
+  return gpa::check_launch("gpa_wait_selftest");
+}
+
 extern "C" int gpa_version(void) { return 100; }
 
 extern "C" const char* gpa_last_error(void) { return gpa::last_error_buf(); }

@@ -181,6 +181,10 @@ __global__ void metric_split_kernel(const T* __restrict__ metric, int64_t stride
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   float nrm = __fsqrt_rn(ss);
+  // a bf16 metric is normalised as torch does it for bf16 tensors (the
+  // reference's GPU run: `metric @ proj` comes out bf16 under autocast): the
+  // norm, accumulated in fp32, is rounded to bf16 before the division
+  if (sizeof(T) == 2) nrm = __bfloat162float(__float2bfloat16_rn(nrm));
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     int ch = lane + c * 32;
@@ -331,6 +335,16 @@ __global__ void select_hist_kernel(const float* __restrict__ node_max, int n, in
     if (sh[i]) atomicAdd(&hist[i], sh[i]);
 }
 
+// threshold state {prefix 0, r still to take} and a zeroed histogram, written on
+// the device so the plan issues no host-to-device copy
+__global__ void select_init_kernel(SelectState* st, unsigned* hist, uint32_t r) {
+  for (int i = threadIdx.x; i < 2048; i += blockDim.x) hist[i] = 0u;
+  if (threadIdx.x == 0) {
+    st->prefix = 0u;
+    st->remaining = r;
+  }
+}
+
 // single thread: walk the histogram from the top bin down
 __global__ void select_pick_kernel(int pass, SelectState* st, unsigned* hist) {
   const int shift = radix_shift(pass), bits = radix_bits(pass);
@@ -376,38 +390,80 @@ __global__ void group_hist_kernel(const int32_t* __restrict__ node_idx, const in
   if (i < n && merged[i]) atomicAdd(&seg_len[node_idx[i]], 1);
 }
 
-__global__ void group_fill_kernel(const int32_t* __restrict__ node_idx, const int* __restrict__ merged,
-                                  const int* __restrict__ unm_rank, int n,
-                                  const int32_t* __restrict__ seg_start, int* __restrict__ cursor,
-                                  int32_t* __restrict__ seg_tmp, int32_t* __restrict__ unm_src) {
+// merged src, in ascending ordinal, go to their merged rank as (key = dst
+// ordinal, value = src ordinal); unmerged src go to unm_src at their unmerged
+// rank, which is the ordinal minus the merged rank
+__global__ void group_compact_kernel(const int32_t* __restrict__ node_idx, const int* __restrict__ merged,
+                                     const int* __restrict__ mrank, int n, int32_t* __restrict__ keys,
+                                     int32_t* __restrict__ vals, int32_t* __restrict__ unm_src) {
   int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
+  const int at = mrank[i];
   if (merged[i]) {
-    int d = node_idx[i];
-    int at = seg_start[d] + atomicAdd(&cursor[d], 1);
-    seg_tmp[at] = i;
+    if (keys) keys[at] = node_idx[i];
+    vals[at] = i;
   } else {
-    unm_src[unm_rank[i]] = i;
+    unm_src[i - at] = i;
   }
 }
 
-// one warp per group: write the group's src ordinals in ascending order
-// (rank sort; groups are short, the quadratic cost only shows on hub groups)
-__global__ void group_sort_kernel(const int32_t* __restrict__ seg_start, int num_dst,
-                                  const int32_t* __restrict__ seg_tmp, int32_t* __restrict__ seg_src,
-                                  float* __restrict__ counts, int unm_len) {
-  int g = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  int lane = threadIdx.x & 31;
-  if (g >= num_dst) return;
-  int s0 = seg_start[g], s1 = seg_start[g + 1];
-  int len = s1 - s0;
-  if (lane == 0) counts[unm_len + g] = (float)(1 + len);
-  for (int k = lane; k < len; k += 32) {
-    int mine = seg_tmp[s0 + k];
-    int rank = 0;
-    for (int j = 0; j < len; ++j) rank += seg_tmp[s0 + j] < mine ? 1 : 0;
-    seg_src[s0 + rank] = mine;
+// Stable LSD radix sort of the merged (dst, src) pairs by dst, 8 bits a pass:
+// a group's members come out in ascending src ordinal without atomics, in time
+// linear in the number of merged src whatever the group sizes.
+constexpr int kRadixItems = 1024;   // pairs per block of one pass
+constexpr int kRadixDigits = 256;
+
+// per block: how many of its pairs fall in each digit -> table[digit][block]
+__global__ void __launch_bounds__(kRadixDigits) radix_hist_kernel(const int32_t* __restrict__ keys, int n,
+                                                                   int shift, int nblk, int* __restrict__ table) {
+  __shared__ int h[kRadixDigits];
+  h[threadIdx.x] = 0;
+  __syncthreads();
+  const int b0 = blockIdx.x * kRadixItems;
+  for (int k = threadIdx.x; k < kRadixItems; k += kRadixDigits) {
+    const int i = b0 + k;
+    if (i < n) atomicAdd(&h[(keys[i] >> shift) & (kRadixDigits - 1)], 1);
   }
+  __syncthreads();
+  table[threadIdx.x * nblk + blockIdx.x] = h[threadIdx.x];
+}
+
+// one warp per block of pairs, 32 at a time in pair order, so equal digits keep
+// their order: lanes with one digit share the digit's running offset and take
+// their rank among themselves; the lowest of them advances the offset
+__global__ void __launch_bounds__(32) radix_scatter_kernel(const int32_t* __restrict__ kin,
+                                                           const int32_t* __restrict__ vin, int n, int shift,
+                                                           int nblk, const int* __restrict__ offsets,
+                                                           int32_t* __restrict__ kout, int32_t* __restrict__ vout) {
+  __shared__ int base[kRadixDigits];
+  const int lane = threadIdx.x;
+  for (int d = lane; d < kRadixDigits; d += 32) base[d] = offsets[d * nblk + blockIdx.x];
+  __syncwarp();
+  const int b0 = blockIdx.x * kRadixItems;
+  for (int c = 0; c < kRadixItems && b0 + c < n; c += 32) {   // warp-uniform
+    const int i = b0 + c + lane;
+    const bool live = i < n;
+    const int key = live ? kin[i] : 0;
+    const int val = live ? vin[i] : 0;
+    const int d = live ? (key >> shift) & (kRadixDigits - 1) : kRadixDigits + lane;
+    const unsigned peers = __match_any_sync(0xffffffffu, d);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    const int pos = live ? base[d] + rank : 0;
+    __syncwarp();
+    if (live && rank == 0) base[d] += __popc(peers);
+    __syncwarp();
+    if (live) {
+      if (kout) kout[pos] = key;
+      vout[pos] = val;
+    }
+  }
+}
+
+// counts of the dst slots: 1 + group size
+__global__ void group_counts_kernel(const int32_t* __restrict__ seg_start, int num_dst,
+                                    float* __restrict__ counts, int unm_len) {
+  int g = blockIdx.x * blockDim.x + threadIdx.x;
+  if (g < num_dst) counts[unm_len + g] = (float)(1 + seg_start[g + 1] - seg_start[g]);
 }
 
 __global__ void ones_f32_kernel(float* __restrict__ f, int n) {
@@ -657,12 +713,15 @@ struct PlanWs {
   unsigned* hist;
   int* block_sums;
   int* flags;    // merged
-  int* eq;       // tie flags
-  int* rank;     // eq rank / unm rank
-  int* seg_len;  // per dst, then cursor
-  int* cursor;
-  int32_t* seg_tmp;
+  int* eq;       // tie flags; later the radix sort's second key buffer
+  int* rank;     // rank among the ties, then merged rank
+  int* seg_len;  // per dst
+  int32_t* key_a;
+  int32_t* val_a;
+  int32_t* val_b;
+  int* table;    // radix digit x block counts, then their offsets
 };
+int radix_blocks(int n) { return (n + kRadixItems - 1) / kRadixItems; }
 int64_t plan_ws_layout(int num_src, int num_dst, char* base, PlanWs* w) {
   int64_t off = 0;
   auto take = [&](int64_t bytes) {
@@ -670,7 +729,9 @@ int64_t plan_ws_layout(int num_src, int num_dst, char* base, PlanWs* w) {
     off += (bytes + 255) & ~int64_t(255);
     return p;
   };
-  int64_t nblk = ((int64_t)std::max(num_src, num_dst + 1) + kScanBlock - 1) / kScanBlock + 1;
+  const int64_t table = (int64_t)kRadixDigits * std::max(1, radix_blocks(num_src));
+  const int64_t scanned = std::max<int64_t>(std::max(num_src, num_dst + 1), table);
+  const int64_t nblk = (scanned + kScanBlock - 1) / kScanBlock + 1;
   PlanWs t;
   t.st = (SelectState*)take(sizeof(SelectState) * 2);
   t.hist = (unsigned*)take(2048 * 4);
@@ -679,8 +740,10 @@ int64_t plan_ws_layout(int num_src, int num_dst, char* base, PlanWs* w) {
   t.eq = (int*)take((int64_t)num_src * 4);
   t.rank = (int*)take((int64_t)num_src * 4);
   t.seg_len = (int*)take((int64_t)(num_dst + 1) * 4);
-  t.cursor = (int*)take((int64_t)num_dst * 4);
-  t.seg_tmp = (int32_t*)take((int64_t)num_src * 4);
+  t.key_a = (int32_t*)take((int64_t)num_src * 4);
+  t.val_a = (int32_t*)take((int64_t)num_src * 4);
+  t.val_b = (int32_t*)take((int64_t)num_src * 4);
+  t.table = (int*)take(table * 4);
   if (w) *w = t;
   return off;
 }
@@ -713,15 +776,15 @@ extern "C" int gpa_merge_plan(const float* node_max, const int32_t* node_idx, in
   const int nb = (num_src + 255) / 256;
   int launched = 0;
 
+  cudaError_t me = cudaSuccess;
   // 1. which src are merged
   if (r == num_src) {
     if (num_src) { fill_ones_kernel<<<nb, 256, 0, st>>>(w.flags, num_src); ++launched; }
   } else if (r == 0) {
-    cudaMemsetAsync(w.flags, 0, (size_t)num_src * 4, st);
+    me = cudaMemsetAsync(w.flags, 0, (size_t)num_src * 4, st);
   } else {
-    SelectState init{0u, (uint32_t)r};
-    cudaMemcpyAsync(w.st, &init, sizeof(init), cudaMemcpyHostToDevice, st);
-    cudaMemsetAsync(w.hist, 0, 2048 * 4, st);
+    select_init_kernel<<<1, 256, 0, st>>>(w.st, w.hist, (uint32_t)r);
+    ++launched;
     int hist_blocks = std::min(1024, (num_src + 1023) / 1024);
     for (int pass = 0; pass < kRadixPasses; ++pass) {
       select_hist_kernel<<<hist_blocks, 256, 0, st>>>(node_max, num_src, pass, w.st, w.hist);
@@ -733,21 +796,42 @@ extern "C" int gpa_merge_plan(const float* node_max, const int32_t* node_idx, in
     select_final_kernel<<<nb, 256, 0, st>>>(num_src, w.st, w.flags, w.eq, w.rank);
     ++launched;
   }
-  // 2. group sizes -> CSR offsets; unmerged ranks
-  cudaMemsetAsync(w.seg_len, 0, (size_t)(num_dst + 1) * 4, st);
-  cudaMemsetAsync(w.cursor, 0, (size_t)num_dst * 4, st);
+  // 2. group sizes -> CSR offsets and counts
+  if (me == cudaSuccess) me = cudaMemsetAsync(w.seg_len, 0, (size_t)(num_dst + 1) * 4, st);
+  if (me != cudaSuccess)
+    return fail(GPA_ERR_CUDA, "gpa_merge_plan: cudaMemsetAsync: %s", cudaGetErrorString(me));
   if (num_src) { group_hist_kernel<<<nb, 256, 0, st>>>(node_idx, w.flags, num_src, w.seg_len); ++launched; }
   launched += exclusive_scan<0>(w.seg_len, seg_start, num_dst + 1, w.block_sums, nullptr, st);
-  if (num_src) {
-    launched += exclusive_scan<1>(w.flags, w.rank, num_src, w.block_sums, nullptr, st);
-    group_fill_kernel<<<nb, 256, 0, st>>>(node_idx, w.flags, w.rank, num_src, seg_start, w.cursor,
-                                          w.seg_tmp, unm_src);
-    ++launched;
-  }
-  // 3. deterministic group order + counts
-  group_sort_kernel<<<(num_dst + 7) / 8, 256, 0, st>>>(seg_start, num_dst, w.seg_tmp, seg_src,
-                                                       counts, unm_len);
+  group_counts_kernel<<<(num_dst + 255) / 256, 256, 0, st>>>(seg_start, num_dst, counts, unm_len);
   ++launched;
+  // 3. members of each group in ascending src ordinal: compact the merged
+  //    (dst, src) pairs in src order, then sort them stably by dst
+  if (num_src) {
+    int passes = 0;
+    for (int bits = 32 - __builtin_clz((unsigned)std::max(num_dst - 1, 1)); bits > 0; bits -= 8) ++passes;
+    if (num_dst == 1) passes = 0;   // one group: src order is the answer
+    launched += exclusive_scan<0>(w.flags, w.rank, num_src, w.block_sums, nullptr, st);
+    int32_t* vals = (passes == 0) ? seg_src : w.val_a;
+    group_compact_kernel<<<nb, 256, 0, st>>>(node_idx, w.flags, w.rank, num_src,
+                                             passes ? w.key_a : nullptr, vals, unm_src);
+    ++launched;
+    const int rblk = radix_blocks(r);
+    int32_t* kin = w.key_a;
+    int32_t* vin = w.val_a;
+    int32_t* kalt = (int32_t*)w.eq;
+    int32_t* valt = w.val_b;
+    for (int pass = 0; pass < passes && r > 0; ++pass) {
+      const bool last = pass + 1 == passes;
+      int32_t* kout = last ? nullptr : kalt;
+      int32_t* vout = last ? seg_src : valt;
+      radix_hist_kernel<<<rblk, kRadixDigits, 0, st>>>(kin, r, 8 * pass, rblk, w.table);
+      launched += 1 + exclusive_scan<0>(w.table, w.table, kRadixDigits * rblk, w.block_sums, nullptr, st);
+      radix_scatter_kernel<<<rblk, 32, 0, st>>>(kin, vin, r, 8 * pass, rblk, w.table, kout, vout);
+      ++launched;
+      kalt = kin; valt = vin;
+      kin = kout; vin = vout;
+    }
+  }
   if (unm_len) { ones_f32_kernel<<<(unm_len + 255) / 256, 256, 0, st>>>(counts, unm_len); ++launched; }
   return check_launch("gpa_merge_plan", launched);
 }
@@ -819,40 +903,30 @@ extern "C" int gpa_merge_kv_mean(const void* t, int dtype, int heads, int n_toke
 // plan's scratch lives in the fixed array below, which the library carries on
 // every GPU that loads it, until the process exits.
 //
-// * The first call on a device looks up the array's device address with
-//   cudaGetSymbolAddress (host code only sees a host-side stand-in under that
-//   name); make that first call before any stream capture on that device.
+// * Every call looks up the array's device address with cudaGetSymbolAddress
+//   on the current device (host code only sees a host-side stand-in under
+//   the array's name).  The lookup is host-only and cheap; doing it on every
+//   call keeps the address right after a cudaDeviceReset or a new primary
+//   context.  The first call on a device may load the library's module onto
+//   that device, so make it before any stream capture on that device.
 // * Every call on a device shares the one array and leaves its last contents
 //   behind; the plan writes or clears every word it reads, so stale contents
 //   never leak into a result, but two calls that overlap on the GPU (other
 //   streams, other host threads) race on the array.
 // * Sizes whose scratch would not fit (gpa_merge_plan_workspace_bytes above
-//   GPA_NOALLOC_SCRATCH_BYTES: about 786k src with 262k dst tokens) are
-//   rejected with GPA_ERR_UNSUPPORTED before anything is launched.
+//   GPA_NOALLOC_SCRATCH_BYTES: about 630k src with 210k dst tokens, which
+//   covers S=500 frames of 37x37 patches) are rejected with
+//   GPA_ERR_UNSUPPORTED before anything is launched.
 // ===========================================================================
-#include <mutex>
-
 namespace {
 static __device__ __align__(256) unsigned char g_plan_scratch[GPA_NOALLOC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_scratch_mu;
-void* g_scratch_addr[kMaxDevices] = {nullptr};
-
 int plan_scratch_for_current_device(void** out) {
-  int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return fail(GPA_ERR_CUDA, "gpa_merge_plan_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
-  if (dev < 0 || dev >= kMaxDevices) return fail(GPA_ERR_UNSUPPORTED, "gpa_merge_plan_noalloc: device %d", dev);
-  std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_addr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_plan_scratch);
-    if (e != cudaSuccess || !p)
-      return fail(GPA_ERR_CUDA, "gpa_merge_plan_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-    g_scratch_addr[dev] = p;
-  }
-  *out = g_scratch_addr[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_plan_scratch);
+  if (e != cudaSuccess || !p)
+    return fail(GPA_ERR_CUDA, "gpa_merge_plan_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+  *out = p;
   return GPA_OK;
 }
 }  // namespace

@@ -18,10 +18,16 @@ from ._lib import call, ptr, stream_of, require_cuda, aligned
 BF16 = torch.bfloat16
 F32 = torch.float32
 
-# GPA_CHECK_STATUS=1: every pipelined kernel gets a device status word that is
-# read back after the launch (synchronises); a nonzero status -- a pipeline
-# wait that gave up -- raises.  Off by default (no host sync on the hot path).
+# Every pipelined kernel (similarity, attention) writes a nonzero code into a
+# device status word when one of its pipeline waits gives up (the kernel then
+# drains what it has in flight and returns, its output invalid).
+# * By default the launches share one persistent word per device, and
+#   check_device_status() reads it at a point that synchronises anyway (the
+#   end of the aggregator's forward): a timed-out wait raises there.
+# * GPA_CHECK_STATUS=1 gives every launch its own word and reads it right after
+#   the launch (synchronises every launch; the tests set it).
 CHECK_STATUS = os.environ.get("GPA_CHECK_STATUS", "0") == "1"
+_DEVICE_STATUS = {}
 
 
 # When set to a list, every attention launch appends (start event, end event,
@@ -33,9 +39,33 @@ class KernelTimeout(RuntimeError):
     """A kernel's pipeline wait gave up (device status word set)."""
 
 
+def device_status_word(device) -> torch.Tensor:
+    """The persistent status word of `device` (int32, zero while all is well)."""
+    dev = torch.device(device)
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    w = _DEVICE_STATUS.get(key)
+    if w is None:
+        w = torch.zeros(1, device=torch.device("cuda", key), dtype=torch.int32)
+        _DEVICE_STATUS[key] = w
+    return w
+
+
+def check_device_status(device, what: str = "forward") -> None:
+    """Read (synchronises) and clear the device's persistent status word;
+    raise KernelTimeout if a kernel recorded a wait that gave up."""
+    w = device_status_word(device)
+    v = int(w.item())
+    if v != 0:
+        w.zero_()
+        raise KernelTimeout(f"{what}: device status {v} (a kernel's pipeline wait gave up; "
+                            "its output is invalid)")
+
+
 def _status_word(status, device):
-    if status is None and CHECK_STATUS:
-        return torch.zeros(1, device=device, dtype=torch.int32), True
+    if status is None:
+        if CHECK_STATUS:
+            return torch.zeros(1, device=device, dtype=torch.int32), True
+        return device_status_word(device), False
     return status, False
 
 
@@ -43,6 +73,15 @@ def _check_status(status, what):
     v = int(status.item())
     if v != 0:
         raise KernelTimeout(f"{what}: device status {v} (a pipeline wait gave up)")
+
+
+def wait_selftest(limit_ns: int, device="cuda") -> None:
+    """Run gpa_wait_selftest (a bounded wait on a barrier nothing arrives on)
+    with its own status word; raises KernelTimeout as a real timeout would."""
+    status = torch.zeros(1, device=device, dtype=torch.int32)
+    call("gpa_wait_selftest", ctypes.c_uint64(int(limit_ns)), ptr(status),
+         _lib._vp(torch.cuda.current_stream(torch.device(device)).cuda_stream))
+    _check_status(status, "gpa_wait_selftest")
 
 
 def _dt(t: torch.Tensor) -> int:
@@ -180,9 +219,16 @@ def merge_kv(t: torch.Tensor, plan: MergePlan, mean: bool = True, out: Optional[
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bias: Optional[torch.Tensor],
               sm_scale: float, return_lse: bool = False, out: Optional[torch.Tensor] = None,
-              status: Optional[torch.Tensor] = None):
+              status: Optional[torch.Tensor] = None, combine=None,
+              lse_out: Optional[torch.Tensor] = None):
     """softmax(q k^T * scale + bias) v for q [B,H,M,64], k/v [B,H,N,64] bf16;
-    bias fp32 broadcastable to [B,H,N] (natural-log domain) or None."""
+    bias fp32 broadcastable to [B,H,N] (natural-log domain) or None.
+
+    combine=(oa, lse_a): another partition of the same softmax -- its
+    normalised output oa [B,H,M,64] bf16 and log2 row sums lse_a [B,H,M] fp32
+    -- merged into the result in the kernel's epilogue (exact two-partition
+    combine); `out` may be oa itself (in place).  lse_out: where the log2 row
+    sums go ([B,H,M] fp32 view, innermost contiguous; implies return_lse)."""
     require_cuda(q, k, v, bias, what="attention")
     for t in (q, k, v):
         if t.dtype != BF16:
@@ -206,18 +252,38 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bias: Optional[
         bsb, bsh = bias.stride(0), bias.stride(1)
     if out is None:
         out = torch.empty(B, H, M, D, device=q.device, dtype=BF16)
-    lse = torch.empty(B, H, M, device=q.device, dtype=F32) if return_lse else None
+    if lse_out is not None:
+        if lse_out.dtype != F32 or tuple(lse_out.shape) != (B, H, M) or lse_out.stride(-1) != 1:
+            raise ValueError("attention: lse_out must be an fp32 [B,H,M] view with row stride 1")
+        lse, return_lse = lse_out, True
+    else:
+        lse = torch.empty(B, H, M, device=q.device, dtype=F32) if return_lse else None
     status, own = _status_word(status, q.device)
     timing = ATTN_TIMING
     if timing is not None:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-    call("gpa_attention_keybias", ptr(q), ptr(k), ptr(v), ptr(bias), B, H, M, N, D,
-         q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
-         v.stride(0), v.stride(1), v.stride(2), bsb, bsh, float(sm_scale), ptr(out),
-         out.stride(0), out.stride(1), out.stride(2), ptr(lse),
-         lse.stride(0) if lse is not None else 0, lse.stride(1) if lse is not None else 0,
-         ptr(status), stream_of(q))
+    if combine is None:
+        call("gpa_attention_keybias", ptr(q), ptr(k), ptr(v), ptr(bias), B, H, M, N, D,
+             q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
+             v.stride(0), v.stride(1), v.stride(2), bsb, bsh, float(sm_scale), ptr(out),
+             out.stride(0), out.stride(1), out.stride(2), ptr(lse),
+             lse.stride(0) if lse is not None else 0, lse.stride(1) if lse is not None else 0,
+             ptr(status), stream_of(q))
+    else:
+        oa, la = combine
+        require_cuda(oa, la, what="attention(combine)")
+        if (oa.dtype != BF16 or la.dtype != F32 or tuple(oa.shape) != (B, H, M, D)
+                or tuple(la.shape) != (B, H, M) or oa.stride(-1) != 1 or la.stride(-1) != 1):
+            raise ValueError("attention: combine needs oa [B,H,M,64] bf16 and lse_a [B,H,M] fp32, "
+                             "innermost contiguous")
+        call("gpa_attention_keybias_combine", ptr(q), ptr(k), ptr(v), ptr(bias), B, H, M, N, D,
+             q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
+             v.stride(0), v.stride(1), v.stride(2), bsb, bsh, float(sm_scale),
+             ptr(oa), oa.stride(0), oa.stride(1), oa.stride(2), ptr(la), la.stride(0), la.stride(1),
+             ptr(out), out.stride(0), out.stride(1), out.stride(2), ptr(lse),
+             lse.stride(0) if lse is not None else 0, lse.stride(1) if lse is not None else 0,
+             ptr(status), stream_of(q))
     if timing is not None:
         e1.record()
         timing.append((e0, e1, 4.0 * B * H * M * N * D, 2.0 * B * H * (2 * M + 2 * N) * D))

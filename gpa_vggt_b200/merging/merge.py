@@ -77,10 +77,21 @@ def build_plan(metric: torch.Tensor, w: int, h: int, sx: int, sy: int, r: int,
         a, b = kernels.metric_split(metric, src_pos, dst_pos)
         if src_pos.numel():
             node_max, node_idx = kernels.sim_argmax(a[None], b[None])
+            node_max = matcher_scores(node_max, metric.dtype)
         else:
             node_max = torch.empty(1, 0, device=dev)
             node_idx = torch.empty(1, 0, device=dev, dtype=torch.int32)
         return kernels.merge_plan(node_max[0], node_idx[0], r, dst_pos, src_pos)
+
+
+def matcher_scores(node_max: torch.Tensor, metric_dtype) -> torch.Tensor:
+    """node_max as the reference's matcher hands it to the edge ranking: in the
+    metric's dtype (fused_similarity.py:112 casts the fp32 maxima to a.dtype,
+    merge.py:13-36 keeps bf16 scores), so a bf16 metric -- the GPU run under
+    autocast -- ranks edges on bf16-rounded maxima.  Kept as fp32 values."""
+    if metric_dtype == torch.bfloat16:
+        return node_max.to(torch.bfloat16).float()
+    return node_max
 
 
 def token_merge_bipartite2d(
@@ -107,15 +118,25 @@ def token_merge_bipartite2d(
         raise ValueError("token_merge_bipartite2d: r must be positive")
     if not metric.is_cuda:
         raise ValueError("token_merge_bipartite2d: CUDA tensors required (no CPU fallback)")
-    plans = [build_plan(metric[bi], w, h, sx, sy, r, no_rand, generator, metric_dim, num_special)
-             for bi in range(B)]
+    tokens_per_img = w * h + num_special
+    num_imgs = N // tokens_per_img
+    assert tokens_per_img * num_imgs == N, (
+        f"Token count doesn't match (w*h+{num_special})*num_imgs: N={N} w={w} h={h}")
+    # one dst draw for the whole batch (merge.py:121-126 draws once; the
+    # matching is then per batch element)
+    rand_idx = None if no_rand else draw_dst_choice(num_imgs, w, h, sx, sy, metric.device, generator)
+    plans = [build_plan(metric[bi], w, h, sx, sy, r, no_rand, None, metric_dim, num_special,
+                        rand_idx=rand_idx) for bi in range(B)]
     n_out = plans[0].n_out
 
     def merge(x: torch.Tensor, mode: str = "mean") -> torch.Tensor:
         """[B, N, C] -> [B, unm_len + num_dst, C]: unmerged src, then dst."""
         if mode not in ("mean", "sum"):
             raise ValueError(f"merge: unsupported mode {mode!r}")
-        outs = [kernels.merge_kv(x[bi][None], plans[bi], mean=(mode == "mean"))[0]
+        C = x.shape[-1]
+        pad = (-C) % 8                 # the kernel moves 8-element chunks
+        xx = torch.nn.functional.pad(x, (0, pad)) if pad else x
+        outs = [kernels.merge_kv(xx[bi][None], plans[bi], mean=(mode == "mean"))[0, :, :C]
                 for bi in range(x.shape[0])]
         return torch.stack(outs, 0)
 

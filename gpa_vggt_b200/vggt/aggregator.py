@@ -10,6 +10,8 @@ from __future__ import annotations
 import torch
 import torch.nn as nn
 
+from .. import kernels
+from ..nvtx import nvtx
 from .dino import DinoVisionTransformer
 from .layers import Block, PositionGetter, RotaryPositionEmbedding2D
 
@@ -106,12 +108,20 @@ class Aggregator(nn.Module):
         P, C = tokens.shape[1], tokens.shape[2]
         taps = []
         for b in range(self.depth):
-            tokens = self.frame_blocks[b](tokens.view(B * S, P, C), pos=pos)
+            with nvtx(f"frame_block_{b}"):
+                tokens = self.frame_blocks[b](tokens.view(B * S, P, C), pos=pos)
             frame_out = tokens.view(B, S, P, C)
             gm = b if merge_window(b, self.merging, self.merge_end, self.early_frame_split,
                                    self.core_blocks, self.core_merge_ratio) else None
-            tokens = self.global_blocks[b](tokens.view(B, S * P, C), pos=pos.view(B, S * P, 2),
-                                           global_merging=gm)
+            attn = self.global_blocks[b].attn
+            kind = "frame_shared" if attn.frame_special else ("merged" if gm is not None else "global")
+            with nvtx(f"global_block_{b}_{kind}"):
+                tokens = self.global_blocks[b](tokens.view(B, S * P, C), pos=pos.view(B, S * P, 2),
+                                               global_merging=gm)
             if b in self.tap_blocks:
                 taps.append(torch.cat([frame_out, tokens.view(B, S, P, C)], -1))
+        if images.is_cuda:
+            # one read of the device's status word per forward: a pipeline wait
+            # that gave up in any kernel above raises here (kernels.py)
+            kernels.check_device_status(images.device, "aggregator forward")
         return taps, self.patch_start_idx

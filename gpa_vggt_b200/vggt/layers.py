@@ -17,7 +17,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .. import kernels
-from ..merging.merge import build_plan, draw_dst_choice, projection_basis
+from ..merging.merge import build_plan, draw_dst_choice, matcher_scores, projection_basis
 
 BF16 = torch.bfloat16
 
@@ -271,7 +271,7 @@ def merged_attention_sharded(x, q, k, v, attn: Attention) -> torch.Tensor:
     b_full = sh.gather_varlen(b, [rd[1] - rd[0] for rd, _ in ranges])
     if s1 > s0:
         nm, ni = kernels.sim_argmax(a[None], b_full[None])
-        nm, ni = nm[0], ni[0]
+        nm, ni = matcher_scores(nm[0], metric.dtype), ni[0]
     else:
         nm = torch.empty(0, device=dev)
         ni = torch.empty(0, device=dev, dtype=torch.int32)
@@ -292,32 +292,39 @@ def merged_attention_sharded(x, q, k, v, attn: Attention) -> torch.Tensor:
 
 def merged_attention(x, q, k, v, attn: Attention) -> torch.Tensor:
     """Query-preserving K/V merging (attention.py:233-268): merge K/V into the
-    dst tokens matched on the 128-d projected x, then attend with +log(count)."""
+    dst tokens matched on the 128-d projected x, then attend with +log(count).
+    With B > 1 the dst pattern is drawn once and each batch element is matched,
+    merged and attended on its own (merge.py:121-126, attention.py:251-253)."""
     B, N, C = x.shape
     H, D = attn.num_heads, attn.head_dim
-    if B != 1:
-        raise NotImplementedError("merged_attention: batch size 1 (the reference's eval setting)")
     if attn.shard is not None and attn.shard.active:
+        if B != 1:
+            raise NotImplementedError("merged_attention: frame sharding runs batch size 1")
         return merged_attention_sharded(x, q, k, v, attn)
     r = int(N * attn.merge_ratio)
-    rand_idx = proj = None
-    gen = None
     if attn.rng_override is not None:
         rand_idx, proj = attn.rng_override
     else:
         gen = torch.Generator(device=x.device)
         gen.manual_seed(33)
-    plan = build_plan(x[0], attn.patch_width, attn.patch_height, attn.merge_grid, attn.merge_grid, r,
-                      False, gen, attn.merge_metric_dim, attn.num_special, rand_idx=rand_idx,
-                      proj=proj)
-    # K keeps its dtype through the merge (fp32 after qk-LayerNorm under autocast),
-    # then both are bf16 for the attention, as attention_keybias casts them.
-    km = kernels.merge_kv(k[0].transpose(0, 1), plan)          # [H, N_m, D]
-    vm = kernels.merge_kv(v[0].transpose(0, 1), plan)
-    bias = plan.counts.log().to(BF16).float()                  # rounded like the reference
-    out = torch.empty(1, N, H, D, device=x.device, dtype=BF16)
-    kernels.attention(q.to(BF16).permute(0, 2, 1, 3), km.to(BF16)[None], vm.to(BF16)[None],
-                      bias[None, None], attn.scale, out=out.permute(0, 2, 1, 3))
+        num_imgs = N // (attn.patch_width * attn.patch_height + attn.num_special)
+        rand_idx = draw_dst_choice(num_imgs, attn.patch_width, attn.patch_height, attn.merge_grid,
+                                   attn.merge_grid, x.device, gen)
+        proj = None
+    out = torch.empty(B, N, H, D, device=x.device, dtype=BF16)
+    for bi in range(B):
+        plan = build_plan(x[bi], attn.patch_width, attn.patch_height, attn.merge_grid,
+                          attn.merge_grid, r, False, None, attn.merge_metric_dim, attn.num_special,
+                          rand_idx=rand_idx, proj=proj)
+        # K keeps its dtype through the merge (fp32 after qk-LayerNorm under
+        # autocast), then both are bf16 for the attention, as attention_keybias
+        # casts them.
+        km = kernels.merge_kv(k[bi].transpose(0, 1), plan)          # [H, N_m, D]
+        vm = kernels.merge_kv(v[bi].transpose(0, 1), plan)
+        bias = plan.counts.log().to(BF16).float()                   # rounded like the reference
+        kernels.attention(q[bi:bi + 1].to(BF16).permute(0, 2, 1, 3), km.to(BF16)[None],
+                          vm.to(BF16)[None], bias[None, None], attn.scale,
+                          out=out[bi:bi + 1].permute(0, 2, 1, 3))
     return out
 
 
@@ -327,8 +334,11 @@ def frame_special_attention(q, k, v, attn: Attention) -> torch.Tensor:
     pooled patch summaries (bias +log size), combined exactly by log-sum-exp.
     q, k, v: [1, N, H, D] bf16 -> [1, N, H, D] bf16."""
     B, N, H, D = q.shape
-    if B != 1:
-        raise NotImplementedError("frame_special_attention: batch size 1")
+    if B != 1:   # batch elements are independent sequences of frames
+        if attn.shard is not None and attn.shard.active:
+            raise NotImplementedError("frame_special_attention: frame sharding runs batch size 1")
+        return torch.cat([frame_special_attention(q[bi:bi + 1], k[bi:bi + 1], v[bi:bi + 1], attn)
+                          for bi in range(B)], 0)
     pts, pw, ph, kp = attn.num_special, attn.patch_width, attn.patch_height, attn.broadcast_pool
     P = pw * ph + pts
     S = N // P                      # this rank's frames
@@ -338,11 +348,13 @@ def frame_special_attention(q, k, v, attn: Attention) -> torch.Tensor:
     if kp <= 0:
         raise NotImplementedError("frame_special_attention: broadcast_pool > 0 only")
     q5, k5, v5 = (t.view(S, P, H, D) for t in (q[0], k[0], v[0]))
-    # (a) own-frame patch keys, batch = frames
-    out_a = torch.empty(S, P, H, D, device=q.device, dtype=BF16)
-    _, lse_a = kernels.attention(q5.permute(0, 2, 1, 3), k5[:, pts:].permute(0, 2, 1, 3),
-                                 v5[:, pts:].permute(0, 2, 1, 3), None, attn.scale,
-                                 return_lse=True, out=out_a.permute(0, 2, 1, 3))
+    # (a) own-frame patch keys, batch = frames: rows written token-major
+    #     [N, H, D] (the layout proj reads), log2 row sums head-major [H, N]
+    out = torch.empty(S, P, H, D, device=q.device, dtype=BF16)
+    lse_a = torch.empty(H, N, device=q.device, dtype=torch.float32)
+    kernels.attention(q5.permute(0, 2, 1, 3), k5[:, pts:].permute(0, 2, 1, 3),
+                      v5[:, pts:].permute(0, 2, 1, 3), None, attn.scale,
+                      out=out.permute(0, 2, 1, 3), lse_out=lse_a.view(H, S, P).permute(1, 0, 2))
     # (b) shared set: specials of every frame, then the pooled summaries
     kh, vh = k[0].transpose(0, 1), v[0].transpose(0, 1)       # [H, N, D] views
     pk, pv, size = kernels.frame_pool(kh, vh, S, ph, pw, pts, kp)
@@ -361,13 +373,11 @@ def frame_special_attention(q, k, v, attn: Attention) -> torch.Tensor:
     sv = torch.cat([spv.permute(2, 0, 1, 3).reshape(H, St * pts, D), pv], 1)
     bias = torch.cat([torch.zeros(H, St * pts, device=q.device), size.log()], 1)
     bias = bias.to(BF16).float()                               # the reference casts it to bf16
-    out_b, lse_b = kernels.attention(q[0].transpose(0, 1)[None], sk[None], sv[None], bias[None],
-                                     attn.scale, return_lse=True)
-    # (c) exact combine into token-major [N, H, D]
-    out = torch.empty(S, P, H, D, device=q.device, dtype=BF16)
-    kernels.lse_combine(out_a.permute(2, 0, 1, 3), lse_a.permute(1, 0, 2),
-                        out_b[0].view(H, S, P, D), lse_b[0].view(H, S, P),
-                        out=out.permute(2, 0, 1, 3))
+    # (c) every query against the shared set, combined exactly with (a) by
+    #     log-sum-exp in the kernel's epilogue, in place in `out`
+    o_tok = out.view(N, H, D).permute(1, 0, 2)[None]           # [1, H, N, D] view
+    kernels.attention(q[0].transpose(0, 1)[None], sk[None], sv[None], bias[None], attn.scale,
+                      out=o_tok, combine=(o_tok, lse_a[None]))
     return out.view(1, N, H, D)
 
 

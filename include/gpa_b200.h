@@ -59,6 +59,17 @@ GPA_API const char* gpa_last_error(void);
 GPA_API int64_t gpa_launch_count(void);
 
 /*
+ * Self-test of the failure path shared by every pipelined kernel (no
+ * counterpart in the reference, which has no device-side waits): one warp
+ * waits on a shared-memory mbarrier that nothing arrives on, with the bounded
+ * wait of the pipelined kernels and a limit of limit_ns (1 us .. 10 s).  The
+ * wait gives up, writes 1 (timeout) to *status (device memory) and the kernel
+ * returns, leaving the context usable.  Used by the tests to exercise the
+ * host-side status check without faulting or hanging a GPU.
+ */
+GPA_API int gpa_wait_selftest(uint64_t limit_ns, int* status, void* stream);
+
+/*
  * Similarity + row argmax (replaces merging/fused_similarity.py:81-112, kernel
  * _sim_argmax_kernel :33-78).  For each batch b and row i of a:
  *   node_max[b,i] = max_j  sum_k a[b,i,k]*b[b,j,k]   (bf16 inputs, fp32 accumulate)
@@ -127,11 +138,12 @@ GPA_API int gpa_merge_plan(const float* node_max, const int32_t* node_idx, int n
  * the scratch is a fixed array of GPA_NOALLOC_SCRATCH_BYTES inside the library
  * on each GPU (held until the process exits), so the call allocates nothing.
  * Meant for hosts that give all device memory to their own arena up front, or
- * FFI callers without an allocator.  The first call on a device resolves the
- * array's address (make it before any stream capture); calls that overlap on
- * the GPU race on the shared array; sizes whose scratch exceeds the array
- * (gpa_merge_plan_workspace_bytes > GPA_NOALLOC_SCRATCH_BYTES, about 786k src
- * with 262k dst tokens) return GPA_ERR_UNSUPPORTED without launching.
+ * FFI callers without an allocator.  Every call resolves the array's device
+ * address on the current device; the first call on a device may load the
+ * library onto it, so make that first call before any stream capture.  Calls
+ * that overlap on the GPU race on the shared array; sizes whose scratch exceeds
+ * the array (gpa_merge_plan_workspace_bytes > GPA_NOALLOC_SCRATCH_BYTES, about
+ * 630k src with 210k dst tokens) return GPA_ERR_UNSUPPORTED without launching.
  */
 #define GPA_NOALLOC_SCRATCH_BYTES (16u << 20)
 GPA_API int gpa_merge_plan_noalloc(const float* node_max, const int32_t* node_idx, int num_src,
@@ -177,6 +189,27 @@ GPA_API int gpa_attention_keybias(const void* q, const void* k, const void* v, c
                           int64_t bias_sh, float sm_scale, void* o, int64_t o_sb, int64_t o_sh,
                           int64_t o_sm, float* lse, int64_t lse_sb, int64_t lse_sh, int* status,
                           void* stream);
+
+/*
+ * The same attention, combined in its epilogue with a second partition of the
+ * same softmax over other keys (replaces the two-partition combine of
+ * vggt/layers/attention.py:164-176 and the bf16 round trip before `proj`,
+ * :229).  oa [batch, heads, m, 64] bf16 (strides oa_sb, oa_sh, oa_sm; multiples
+ * of 8) is that partition's normalised output and lse_a [batch, heads, m] fp32
+ * (strides lse_a_sb, lse_a_sh, row stride 1) its log2 row sums.  Each row
+ * becomes o = (wa*oa + wb*ob) / (wa + wb), wa = 2^(lse_a - mx),
+ * wb = 2^(lse_b - mx), mx = max(lse_a, lse_b), with ob and lse_b this call's
+ * attention; lse, if given, receives the log2 row sums of the union.  o may be
+ * the same memory as oa (every row is read before it is written), so the
+ * frame blocks combine in place in the token-major layout `proj` reads.
+ */
+GPA_API int gpa_attention_keybias_combine(
+    const void* q, const void* k, const void* v, const float* bias, int batch, int heads, int m, int n,
+    int head_dim, int64_t q_sb, int64_t q_sh, int64_t q_sm, int64_t k_sb, int64_t k_sh, int64_t k_sn,
+    int64_t v_sb, int64_t v_sh, int64_t v_sn, int64_t bias_sb, int64_t bias_sh, float sm_scale,
+    const void* oa, int64_t oa_sb, int64_t oa_sh, int64_t oa_sm, const float* lse_a, int64_t lse_a_sb,
+    int64_t lse_a_sh, void* o, int64_t o_sb, int64_t o_sh, int64_t o_sm, float* lse, int64_t lse_sb,
+    int64_t lse_sh, int* status, void* stream);
 
 /*
  * Content-adaptive pooling of each frame's patch keys/values (replaces

@@ -8,10 +8,20 @@ import torch
 from oracle import gpa_oracle as O
 
 
-def attention(q, k, v, bias, sm_scale, return_lse=False, out=None, status=None):
+def attention(q, k, v, bias, sm_scale, return_lse=False, out=None, status=None, combine=None,
+              lse_out=None):
     b = None if bias is None else bias.reshape(bias.shape[0], bias.shape[1], 1, -1)
-    res = O.attention_keybias(q, k, v, b, sm_scale, return_lse=True)
-    o, lse = res[0].to(q.dtype), res[1].float()
+    o, lse = O.attention_keybias(q, k, v, b, sm_scale, return_lse=True)
+    if combine is not None:                   # exact two-partition combine
+        oa, la = combine
+        mx = torch.maximum(la.double(), lse)
+        wa, wb = torch.exp2(la.double() - mx), torch.exp2(lse - mx)
+        o = O.lse_combine(oa, la.double(), o, lse)
+        lse = mx + torch.log2(wa + wb)
+    o, lse = o.to(q.dtype), lse.float()
+    if lse_out is not None:
+        lse_out.copy_(lse)
+        lse, return_lse = lse_out, True
     if out is not None:
         out.copy_(o)
         o = out
@@ -29,7 +39,7 @@ def merge_roles(rand_idx, num_imgs, w, h, sx, sy, num_special, no_rand, device):
 
 
 def metric_split(metric, src_pos, dst_pos):
-    m = O.normalize_rows(metric.float())
+    m = O.normalize_rows(metric)
     return m[src_pos.long()].to(torch.bfloat16), m[dst_pos.long()].to(torch.bfloat16)
 
 

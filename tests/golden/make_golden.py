@@ -1,8 +1,14 @@
 """Generate the golden vectors in tests/golden/ from the reference itself.
 
-Run in a container that has the reference checkout (noheat61/GPA-VGGT):
+Run in a container that has the reference checkout (noheat61/GPA-VGGT); the
+path is required:
 
-    GPA_REF=/path/to/GPA-VGGT python tests/golden/make_golden.py
+    GPA_REF=/path/to/GPA-VGGT python tests/golden/make_golden.py [what]
+
+what: (none) the small kernel/merge/attention/frame/block fixtures;
+      config1 (one merged block at BASELINE config 1: S=4, 37x37, dim 1024);
+      model [S] / model_bf16 [S] (full forward, GPA; S=2 by default);
+      vanilla [S] / vanilla_bf16 [S] (full forward, vanilla global attention).
 
 What it runs, all on CPU:
   * merging/merge.py: token_merge_bipartite2d, with its matcher replaced by the
@@ -28,7 +34,9 @@ os.environ.setdefault("TRITON_INTERPRET", "1")
 
 import torch  # noqa: E402
 
-REF = os.environ.get("GPA_REF", "/root/reference")
+REF = os.environ.get("GPA_REF")
+if not REF:
+    sys.exit("make_golden.py: set GPA_REF to the reference checkout (noheat61/GPA-VGGT)")
 OUT = Path(__file__).resolve().parent
 sys.path.insert(0, REF)
 
@@ -253,16 +261,41 @@ def gen_block():
                     out_merged=out_merged[0], out_plain=out_plain[0]), OUT / "block_small.pt")
 
 
-def gen_model_bf16(S=2):
-    """The reference's own bf16 drift: the same forward as gen_model, with the
-    model in bf16 under CPU bf16 autocast, stored beside the fp32 result."""
+def _ref_model(vanilla, bf16):
     sys.path.insert(0, str(OUT.parents[1]))
     from gpa_vggt_b200.vggt.model import init_weights
     from vggt.models.vggt import VGGT as RefVGGT
-    model = RefVGGT()
+    torch.manual_seed(0)
+    model = RefVGGT(merging=None, early_frame_split=0) if vanilla else RefVGGT()
     init_weights(model, seed=0)
-    model = model.eval().to(torch.bfloat16)
+    model = model.eval()
+    if bf16:
+        model = model.to(torch.bfloat16)
     model.update_patch_dimensions(37, 37)
+    return model
+
+
+def _store(out, S, depth_stride):
+    """pose encoding in full; depth and confidence every depth_stride-th pixel
+    in each direction (fp16), which keeps the S=10 fixture near 1 MB."""
+    st = depth_stride
+    return dict(pose_enc=out["pose_enc"].float().clone(),
+                depth=out["depth"].float()[:, :, ::st, ::st].half().clone(),
+                depth_conf=out["depth_conf"].float()[:, :, ::st, ::st].half().clone(),
+                depth_stride=st)
+
+
+def gen_model(S=2, vanilla=False, bf16=False):
+    """Full VGGT forward on CPU with the weights of
+    gpa_vggt_b200.vggt.init_weights(seed=0) (a function of parameter names and
+    shapes only, so the GPU test rebuilds the same weights) on
+    torch.rand(1, S, 3, 518, 518) frames (CPU generator seed 0).  GPA
+    configuration, or vanilla global attention (merging=None,
+    early_frame_split=0).  fp32, or with bf16 the model in bf16 under CPU
+    autocast: the reference's own bf16 drift, which sets the GPU test's
+    tolerance.  The matcher is the reference's Triton kernel under the
+    interpreter (the GPU contract)."""
+    model = _ref_model(vanilla, bf16)
     images = torch.rand(1, S, 3, 518, 518, generator=torch.Generator().manual_seed(0))
     stock = ref_merge.fast_similarity_chunks
 
@@ -272,60 +305,116 @@ def gen_model_bf16(S=2):
 
     ref_merge.fast_similarity_chunks = matcher
     try:
-        with torch.no_grad(), torch.autocast("cpu", dtype=torch.bfloat16):
-            out = model(images.to(torch.bfloat16))
-    finally:
-        ref_merge.fast_similarity_chunks = stock
-    torch.save(dict(S=S, pose_enc=out["pose_enc"].float().clone(),
-                    depth=out["depth"].half().clone(), depth_conf=out["depth_conf"].half().clone()),
-               OUT / f"model_s{S}_bf16.pt")
-
-
-def gen_model(S=2):
-    """Full VGGT (GPA configuration) forward on CPU, fp32, with the weights of
-    gpa_vggt_b200.vggt.init_weights(seed=0) (a function of parameter names and
-    shapes only, so the GPU test rebuilds the same weights)."""
-    sys.path.insert(0, str(OUT.parents[1]))
-    from gpa_vggt_b200.vggt.model import init_weights
-    from vggt.models.vggt import VGGT as RefVGGT
-    torch.manual_seed(0)
-    model = RefVGGT()
-    init_weights(model, seed=0)
-    model.eval()
-    model.update_patch_dimensions(37, 37)
-    images = torch.rand(1, S, 3, 518, 518, generator=torch.Generator().manual_seed(0))
-    stock = ref_merge.fast_similarity_chunks
-
-    def matcher(a, bT, chunk):
-        nm, ni = interp_sim_argmax(a, bT.transpose(-1, -2))
-        return nm.to(a.dtype), ni
-
-    ref_merge.fast_similarity_chunks = matcher
-    try:
         with torch.no_grad():
-            out = model(images)
+            if bf16:
+                with torch.autocast("cpu", dtype=torch.bfloat16):
+                    out = model(images.to(torch.bfloat16))
+            else:
+                out = model(images)
     finally:
         ref_merge.fast_similarity_chunks = stock
     g = torch.Generator().manual_seed(33)
     rand_idx = torch.randint(4, size=(S - 1, 18, 18), generator=g)
     gp = torch.Generator().manual_seed(ref_merge.PROJ_SEED)
     proj = torch.randn(1024, 128, dtype=torch.float32, generator=gp)
-    torch.save(dict(S=S, image_seed=0, weight_seed=0, rand_idx=rand_idx, proj=proj,
-                    pose_enc=out["pose_enc"].clone(),
-                    depth=out["depth"].half().clone(), depth_conf=out["depth_conf"].half().clone()),
-               OUT / f"model_s{S}.pt")
+    rec = dict(S=S, image_seed=0, weight_seed=0, vanilla=vanilla, rand_idx=rand_idx, proj=proj)
+    rec.update(_store(out, S, 1 if S <= 2 else 2))
+    name = f"{'vanilla' if vanilla else 'model'}_s{S}{'_bf16' if bf16 else ''}.pt"
+    torch.save(rec, OUT / name)
+    print(name, (OUT / name).stat().st_size)
+
+
+def gen_config1():
+    """One GPA merged global block at BASELINE config 1: S=4 frames of
+    1 + 4 + 37x37 tokens (N=5,496), dim 1024, 16 heads x 64, x ~ N(0,1) from a
+    CPU generator seeded 0; the reference's Attention (qk-LayerNorm, 2-D RoPE
+    at frequency 100) with init_weights(seed=0), merge ratio 0.98, metric dim
+    128; its forward(x, pos, global_merging=9) on CPU in fp32, the matcher
+    being the reference's Triton kernel under the interpreter.  Stored: the
+    metric the matcher saw (bf16 values), the match, the merge map keyed by
+    absolute position, and every 8th row of the block output (fp16), also of
+    the same forward in bf16 under CPU autocast (the reference's bf16 drift)."""
+    sys.path.insert(0, str(OUT.parents[1]))
+    from gpa_vggt_b200.vggt.model import init_weights
+    S, w, h, ns, C, H = 4, 37, 37, 5, 1024, 16
+    P = w * h + ns
+    N = S * P
+    attn = Attention(C, num_heads=H, qk_norm=True, rope=RotaryPositionEmbedding2D(frequency=100),
+                     patch_width=w, patch_height=h, merge_ratio=0.98)
+    attn.merge_metric_dim = 128
+    init_weights(attn, seed=0)
+    attn.eval()
+    x = torch.randn(1, N, C, generator=torch.Generator().manual_seed(0))
+    pos = PositionGetter()(S, h, w, device="cpu") + 1
+    pos = torch.cat([torch.zeros(S, ns, 2, dtype=pos.dtype), pos], 1).reshape(1, N, 2)
+    cap = {}
+    stock = ref_merge.fast_similarity_chunks
+
+    def matcher(a, bT, chunk):
+        cap["a"], cap["b"] = bf16v(a).clone(), bf16v(bT.transpose(-1, -2)).clone()
+        nm, ni = interp_sim_argmax(a, bT.transpose(-1, -2))
+        cap["node_max"], cap["node_idx"] = nm.clone(), ni.clone()
+        return nm.to(a.dtype), ni
+
+    ref_merge.fast_similarity_chunks = matcher
+    sorts = []
+    argsort = torch.Tensor.argsort
+
+    def capture_argsort(self, *a, **k):
+        out = argsort(self, *a, **k)
+        sorts.append(out.clone())
+        return out
+
+    torch.Tensor.argsort = capture_argsort
+    try:
+        with torch.no_grad():
+            out = attn(x, pos=pos, global_merging=9)
+    finally:
+        ref_merge.fast_similarity_chunks = stock
+        torch.Tensor.argsort = argsort
+    num_dst = cap["b"].shape[1]
+    a_idx = sorts[0].reshape(-1)[num_dst:]          # src positions in the matcher's row order
+    b_idx = sorts[0].reshape(-1)[:num_dst]          # dst positions in its column order
+    dst_of_src = torch.full((N,), -1, dtype=torch.long)
+    dst_of_src[a_idx] = b_idx[cap["node_idx"].reshape(-1)]
+    g = torch.Generator().manual_seed(33)
+    rand_idx = torch.randint(4, size=(S - 1, h // 2, w // 2), generator=g)
+    gp = torch.Generator().manual_seed(ref_merge.PROJ_SEED)
+    proj = torch.randn(C, 128, dtype=torch.float32, generator=gp)
+    # the reference's own bf16 drift at this block: the same forward with the
+    # module in bf16 under CPU autocast (sets the GPU test's tolerance)
+    ref_merge.fast_similarity_chunks = lambda a_, bT_, c_: tuple(
+        t.to(a_.dtype) if i == 0 else t
+        for i, t in enumerate(interp_sim_argmax(a_.float(), bT_.transpose(-1, -2).float())))
+    try:
+        attn16 = attn.to(torch.bfloat16)
+        with torch.no_grad(), torch.autocast("cpu", dtype=torch.bfloat16):
+            out16 = attn16(x.to(torch.bfloat16), pos=pos, global_merging=9).float()
+    finally:
+        ref_merge.fast_similarity_chunks = stock
+    rows = torch.arange(0, N, 8)
+    torch.save(dict(S=S, w=w, h=h, num_special=ns, heads=H, x_seed=0, weight_seed=0, ratio=0.98,
+                    rand_idx=rand_idx, proj=proj,
+                    a=cap["a"][0].bfloat16(), b=cap["b"][0].bfloat16(),
+                    a_pos=a_idx.int(), b_pos=b_idx.int(),
+                    node_max=cap["node_max"].reshape(-1), node_idx=cap["node_idx"].reshape(-1).int(),
+                    dst_of_src=dst_of_src.int(), rows=rows, out_rows=out[0, rows].half().clone(),
+                    out_rows_bf16=out16[0, rows].half().clone()),
+               OUT / "config1_block.pt")
+    print("config1_block.pt", (OUT / "config1_block.pt").stat().st_size)
 
 
 if __name__ == "__main__":
-    if len(sys.argv) > 1 and sys.argv[1] == "model":
-        gen_model()
-        sys.exit(0)
-    if len(sys.argv) > 1 and sys.argv[1] == "model_bf16":
-        gen_model_bf16()
-        sys.exit(0)
-    gen_merge()
-    gen_attention()
-    gen_frame()
-    gen_block()
-    for f in sorted(OUT.glob("*.pt")):
-        print(f.name, f.stat().st_size)
+    what = sys.argv[1] if len(sys.argv) > 1 else ""
+    n = int(sys.argv[2]) if len(sys.argv) > 2 else 2
+    if what == "config1":
+        gen_config1()
+    elif what in ("model", "model_bf16", "vanilla", "vanilla_bf16"):
+        gen_model(n, vanilla=what.startswith("vanilla"), bf16=what.endswith("bf16"))
+    else:
+        gen_merge()
+        gen_attention()
+        gen_frame()
+        gen_block()
+        for f in sorted(OUT.glob("*.pt")):
+            print(f.name, f.stat().st_size)

@@ -15,14 +15,7 @@ def _oracle_kernels(monkeypatch, rand_idx, proj):
     from gpa_vggt_b200 import kernels
     from gpa_vggt_b200.vggt import layers
 
-    def attention(q, k, v, bias, sm_scale, return_lse=False, out=None, status=None):
-        b = None if bias is None else bias.reshape(bias.shape[0], bias.shape[1], 1, -1)
-        res = O.attention_keybias(q, k, v, b, sm_scale, return_lse=True)
-        o, lse = res[0].to(q.dtype), res[1].float()
-        if out is not None:
-            out.copy_(o)
-            o = out
-        return (o, lse) if return_lse else o
+    from cpu_kernels import attention   # noqa: E402 (tests/ is on sys.path under pytest)
 
     def build_plan(metric, w, h, sx, sy, r, no_rand=False, generator=None, metric_dim=0,
                    num_special=5, rand_idx=None, proj=None):

@@ -1,0 +1,224 @@
+"""This path against the reference's own GPU path on the same B200.
+
+The reference (noheat61/GPA-VGGT, unmodified) is installed offline into
+baseline/_ref (git-ignored; it travels to the GPU box with the tree); these
+tests are skipped where it is absent.  Both sides get identical CUDA inputs and
+make the same CUDA RNG draws (generator seeded 33 for the dst pick, 1234 for
+the projection), as the reference's Attention.forward does on a GPU
+(attention.py:238-249, merge.py:121-126, :180-184).  The reference's matcher and
+attention are its Triton kernels (fused_similarity.py, fused_attention.py).
+
+* token_merge_bipartite2d at S = 10 and S = 200 (274,800 tokens: the
+  production size), ratios 0.98 and 0.2: the dst/src split equal; the match of
+  every src row equal except rows whose exact top-2 gap is below 1e-6; at
+  ratio 0.2 the merged set equal except inside the tie group at the cut; counts
+  keyed by dst position equal where the matches are;
+* merge.heads of K (fp32) and V (bf16) at S = 10: K within fp32 rounding of
+  the reference's; V at least as close to the exact float64 mean as the
+  reference's (its bf16 atomics round after every addition);
+* attention_keybias at a merged shape (16 heads, 13,740 queries, 4,335 keys,
+  bias log(count)): the two kernels within rel-L2 1e-2 of each other.
+"""
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+REF = ROOT / "baseline" / "_ref"
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not (REF / "merging" / "merge.py").exists(),
+                                 reason="the reference is not installed in baseline/_ref")]
+
+DEV = "cuda"
+P_TOK = 37 * 37 + 5
+
+
+@pytest.fixture(scope="module")
+def ref():
+    from gpa_vggt_b200 import build, _lib
+    build.build()
+    _lib.load()
+    if str(REF) not in sys.path:
+        sys.path.insert(0, str(REF))
+    import merging.merge as ref_merge              # noqa: E402 (the reference's package)
+    import merging.fused_attention as ref_fa       # noqa: E402
+    return ref_merge, ref_fa
+
+
+def _gen(seed):
+    g = torch.Generator(device=DEV)
+    g.manual_seed(seed)
+    return g
+
+
+def _merge_both(ref_merge, x, r):
+    from gpa_vggt_b200.merging.merge import token_merge_bipartite2d
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        mr = ref_merge.token_merge_bipartite2d(x, 37, 37, 2, 2, r, False, _gen(33), metric_dim=128,
+                                               num_special=5)
+        mo = token_merge_bipartite2d(x, 37, 37, 2, 2, r, False, _gen(33), metric_dim=128,
+                                     num_special=5)
+    return mr, mo
+
+
+def _closure(fn):
+    return {n: c.cell_contents for n, c in zip(fn.__code__.co_freevars, fn.__closure__)}
+
+
+def _metric(x):
+    """The normalised bf16 metric the reference's matcher sees (merge.py:180-187
+    under autocast), for the exact top-2 gaps."""
+    g = torch.Generator(device=DEV)
+    g.manual_seed(1234)
+    proj = torch.randn(x.shape[-1], 128, device=DEV, dtype=torch.float32, generator=g).to(x.dtype)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        m = x[0] @ proj
+    return (m / m.norm(dim=-1, keepdim=True)).bfloat16()
+
+
+def _top2_gap(a, b, rows):
+    """Exact (float64) top-2 gap of the given src rows against every dst row."""
+    bd = b.double()
+    out = torch.empty(rows.numel(), dtype=torch.float64, device=DEV)
+    for i in range(0, rows.numel(), 2048):
+        s = a[rows[i:i + 2048]].double() @ bd.T
+        t = s.topk(2, dim=1).values
+        out[i:i + 2048] = t[:, 0] - t[:, 1]
+    return out
+
+
+def _maps(mr, mo, N):
+    """Per absolute position: the dst position each merged src goes to, in the
+    reference's merge and in ours, and which src each merged."""
+    cv = _closure(mr)
+    plan = mo.plans[0]
+    b_idx = cv["b_idx"].reshape(-1)
+    ref_dst_of = torch.full((N,), -1, dtype=torch.long, device=DEV)
+    ref_dst_of[cv["src_abs_idx"].reshape(-1)] = b_idx[cv["dst_idx"].reshape(-1)]
+    merged_ord = torch.ones(plan.num_src, dtype=torch.bool, device=DEV)
+    merged_ord[plan.unm_src.long()] = False
+    ours_dst_of = torch.full((N,), -1, dtype=torch.long, device=DEV)
+    src = plan.src_pos.long()[merged_ord]
+    ours_dst_of[src] = plan.dst_pos.long()[plan.node_idx.reshape(-1).long()[merged_ord]]
+    return cv, plan, ref_dst_of, ours_dst_of
+
+
+@pytest.mark.parametrize("S,ratio", [(10, 0.98), (10, 0.2), (200, 0.98), (200, 0.2)])
+def test_merge_plan_matches_reference_gpu_path(ref, S, ratio):
+    ref_merge, _ = ref
+    N = S * P_TOK
+    x = torch.randn(1, N, 1024, device=DEV, generator=_gen(S)).bfloat16()
+    r = int(N * ratio)
+    mr, mo = _merge_both(ref_merge, x, r)
+    cv, plan, ref_dst_of, ours_dst_of = _maps(mr, mo, N)
+    # dst/src split (merge.py:87-176)
+    b_idx = cv["b_idx"].reshape(-1)
+    assert torch.equal(b_idx.sort().values.int(), plan.dst_pos)
+    src_abs = torch.cat([cv["unm_abs_idx"].reshape(-1), cv["src_abs_idx"].reshape(-1)])
+    assert torch.equal(src_abs.sort().values.int(), plan.src_pos)
+    # the merged set: the top r of node_max (the reference's argsort is
+    # unstable and its fp32 sums run in another order, so the sets may differ
+    # only among src whose node_max is within 1e-6 of the cut)
+    ref_merged, ours_merged = ref_dst_of >= 0, ours_dst_of >= 0
+    if r < plan.num_src:
+        nm = plan.node_max.reshape(-1)
+        cut = nm.sort(descending=True).values[r - 1]
+        near = torch.zeros(N, dtype=torch.bool, device=DEV)
+        near[plan.src_pos.long()] = (nm - cut).abs() <= 1e-6
+        assert int(((ref_merged != ours_merged) & ~near).sum()) == 0
+    else:
+        assert torch.equal(ref_merged, ours_merged)
+    # each merged src's match, keyed by absolute position: equal except on
+    # rows whose exact top-2 gap is below 1e-6
+    both = ref_merged & ours_merged
+    diff = both & (ref_dst_of != ours_dst_of)
+    m = _metric(x)
+    a, b = m[plan.src_pos.long()], m[plan.dst_pos.long()]
+    rows_ord = torch.full((N,), -1, dtype=torch.long, device=DEV)
+    rows_ord[plan.src_pos.long()] = torch.arange(plan.num_src, device=DEV)
+    bad_rows = rows_ord[diff.nonzero().reshape(-1)]
+    gaps = _top2_gap(a, b, bad_rows) if bad_rows.numel() else torch.zeros(0, device=DEV)
+    print(f"S={S} ratio={ratio}: {int(diff.sum())} of {int(both.sum())} merged rows matched "
+          f"differently; largest top-2 gap among them {float(gaps.max()) if gaps.numel() else 0:.2e}")
+    assert int((gaps >= 1e-6).sum()) == 0
+    # counts keyed by dst position, where no differing src is involved
+    ref_size = mr.size.reshape(-1)
+    unm_len = ref_size.numel() - b_idx.numel()
+    ref_cnt = torch.zeros(N, device=DEV)
+    ref_cnt[b_idx] = ref_size[unm_len:]
+    ours_cnt = torch.zeros(N, device=DEV)
+    ours_cnt[plan.dst_pos.long()] = plan.counts[plan.unm_len:]
+    odd = diff | (ref_merged != ours_merged)
+    touched = torch.zeros(N, dtype=torch.bool, device=DEV)
+    touched[ref_dst_of[odd & ref_merged]] = True
+    touched[ours_dst_of[odd & ours_merged]] = True
+    keep = torch.zeros(N, dtype=torch.bool, device=DEV)
+    keep[plan.dst_pos.long()] = True
+    keep &= ~touched
+    assert torch.equal(ref_cnt[keep], ours_cnt[keep])
+
+
+def test_merge_heads_match_reference_gpu_path(ref):
+    """K (fp32) and V (bf16) scatter-means, dst slots keyed by position (ratio
+    0.98 merges every src).  K: within fp32 rounding of the reference.  V: the
+    reference's bf16 atomics round after every addition, ours sums in fp32;
+    ours must be at least as close to the exact float64 mean."""
+    ref_merge, _ = ref
+    S = 10
+    N = S * P_TOK
+    x = torch.randn(1, N, 1024, device=DEV, generator=_gen(5)).bfloat16()
+    k = torch.randn(1, 16, N, 64, device=DEV, generator=_gen(6))             # fp32, as after qk-LN
+    v = torch.randn(1, 16, N, 64, device=DEV, generator=_gen(7)).bfloat16()
+    mr, mo = _merge_both(ref_merge, x, int(N * 0.98))
+    cv, plan, ref_dst_of, ours_dst_of = _maps(mr, mo, N)
+    b_idx = cv["b_idx"].reshape(-1)
+    order = b_idx.argsort()
+    with torch.no_grad():
+        kr, vr = mr.heads(k)[0][:, order], mr.heads(v)[0][:, order]
+        ko, vo = mo.heads(k)[0], mo.heads(v)[0]
+    # slots whose members match alike on both sides
+    diff = ref_dst_of != ours_dst_of
+    bad = torch.zeros(N, dtype=torch.bool, device=DEV)
+    bad[ref_dst_of[diff & (ref_dst_of >= 0)]] = True
+    bad[ours_dst_of[diff & (ours_dst_of >= 0)]] = True
+    keep = ~bad[plan.dst_pos.long()]
+    assert float(keep.float().mean()) > 0.99
+    kr, ko, vr, vo = kr[:, keep], ko[:, keep], vr[:, keep], vo[:, keep]
+    assert float((kr - ko).abs().max()) <= 1e-5 * float(kr.abs().max())
+    exact = torch.zeros(16, N, 64, device=DEV, dtype=torch.float64)
+    cnt = torch.zeros(N, device=DEV, dtype=torch.float64)
+    vt = v[0].double()
+    dpos = plan.dst_pos.long()
+    exact[:, dpos] = vt[:, dpos]
+    cnt[dpos] = 1
+    src = (ours_dst_of >= 0).nonzero().reshape(-1)
+    exact.index_add_(1, ours_dst_of[src], vt[:, src])
+    cnt.index_add_(0, ours_dst_of[src], torch.ones(src.numel(), device=DEV, dtype=torch.float64))
+    exact = (exact[:, dpos] / cnt[dpos][None, :, None])[:, keep]
+    e_ours = float((vo.double() - exact).norm() / exact.norm())
+    e_ref = float((vr.double() - exact).norm() / exact.norm())
+    print(f"merged V vs exact mean: ours {e_ours:.2e}, reference {e_ref:.2e}")
+    assert e_ours <= e_ref * 1.01 + 1e-7
+
+
+def test_attention_keybias_matches_reference_triton_kernel(ref):
+    from gpa_vggt_b200.merging.fused_attention import attention_keybias
+    _, ref_fa = ref
+    M, N, H, D = 13740, 4335, 16, 64
+    g = _gen(11)
+    q = torch.randn(1, H, M, D, device=DEV, generator=g).bfloat16()
+    k = torch.randn(1, H, N, D, device=DEV, generator=g).bfloat16()
+    v = torch.randn(1, H, N, D, device=DEV, generator=g).bfloat16()
+    cnt = 1 + torch.poisson(torch.ones(N, device=DEV), generator=g)
+    bias = cnt.log().bfloat16().reshape(1, 1, 1, N).expand(1, H, 1, N).contiguous()
+    with torch.no_grad():
+        o_ref, lse_ref = ref_fa.attention_keybias(q, k, v, bias, D ** -0.5, return_lse=True)
+        o, lse = attention_keybias(q, k, v, bias, D ** -0.5, return_lse=True)
+    err = float((o.double() - o_ref.double()).norm() / o_ref.double().norm())
+    print(f"attention vs the reference's Triton kernel: rel-L2 {err:.2e}, "
+          f"max |dlse| {float((lse - lse_ref).abs().max()):.2e}")
+    assert err < 1e-2
+    assert float((lse - lse_ref).abs().max()) < 2e-3

@@ -68,6 +68,32 @@ def test_noalloc_plan_matches_workspace_plan_twice_in_a_row(lib, ns, nd, ratios,
         assert torch.equal(counts, want.counts)
 
 
+def test_noalloc_plan_allocates_nothing(lib):
+    """After a first call, a call changes neither torch's allocation count nor
+    the device's free memory (cudaMemGetInfo): the scratch is the library's
+    fixed array, not an allocation."""
+    from gpa_vggt_b200 import _lib
+    ns, nd = 207955, 66845
+    node_max, node_idx = _inputs(ns, nd, 5)
+    r = int((ns + nd) * 0.2)
+    unm = torch.empty(ns - r, device=DEV, dtype=torch.int32)
+    seg_start = torch.empty(nd + 1, device=DEV, dtype=torch.int32)
+    seg_src = torch.empty(r, device=DEV, dtype=torch.int32)
+    counts = torch.empty(ns - r + nd, device=DEV)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    args = (_lib.ptr(node_max), _lib.ptr(node_idx), ns, nd, r, _lib.ptr(unm), _lib.ptr(seg_start),
+            _lib.ptr(seg_src), _lib.ptr(counts), stream)
+    _lib.check(lib.gpa_merge_plan_noalloc(*args), "gpa_merge_plan_noalloc")   # warm-up
+    torch.cuda.synchronize()
+    n_alloc = torch.cuda.memory_stats()["allocation.all.allocated"]
+    free0, _ = torch.cuda.mem_get_info()
+    _lib.check(lib.gpa_merge_plan_noalloc(*args), "gpa_merge_plan_noalloc")
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert torch.cuda.memory_stats()["allocation.all.allocated"] == n_alloc
+    assert free1 == free0
+
+
 def test_noalloc_plan_rejects_sizes_beyond_its_scratch(lib):
     from gpa_vggt_b200 import _lib
     big = 4_000_000
