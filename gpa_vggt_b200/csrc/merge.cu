@@ -180,11 +180,11 @@ __global__ void metric_split_kernel(const T* __restrict__ metric, int64_t stride
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  // fp32 norm and quotient, rounded to bf16 once: the reference's GPU run under
+  // autocast computes `metric.norm()` in fp32 (norm is on autocast's fp32
+  // list), so `metric / norm` is an fp32 division even for a bf16 metric, and
+  // the matcher casts the quotient to bf16 (fused_similarity.py:99-101)
   float nrm = __fsqrt_rn(ss);
-  // a bf16 metric is normalised as torch does it for bf16 tensors (the
-  // reference's GPU run: `metric @ proj` comes out bf16 under autocast): the
-  // norm, accumulated in fp32, is rounded to bf16 before the division
-  if (sizeof(T) == 2) nrm = __bfloat162float(__float2bfloat16_rn(nrm));
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     int ch = lane + c * 32;
@@ -842,8 +842,11 @@ extern "C" int gpa_merge_kv_mean(const void* t, int dtype, int heads, int n_toke
                                  const int32_t* seg_start, const int32_t* seg_src, int num_dst,
                                  int reduce_mean, float* log_counts, void* out,
                                  int64_t out_stride_h, int64_t out_stride_n, void* stream) {
-  if (heads <= 0 || head_dim <= 0 || head_dim % 8 || n_tokens <= 0 || unm_len < 0 || num_dst <= 0)
+  if (heads <= 0 || head_dim <= 0 || head_dim % 8 || n_tokens <= 0 || unm_len < 0 || num_dst < 0 ||
+      unm_len + num_dst <= 0)
     return fail(GPA_ERR_INVALID, "gpa_merge_kv_mean: bad sizes (head_dim %% 8 == 0)");
+  if ((unm_len && (!src_pos || !unm_src)) || (num_dst && (!dst_pos || !seg_start || !src_pos)))
+    return fail(GPA_ERR_INVALID, "gpa_merge_kv_mean: null index array");
   if (t_stride_h % 8 || t_stride_n % 8 || out_stride_h % 8 || out_stride_n % 8)
     return fail(GPA_ERR_INVALID, "gpa_merge_kv_mean: strides must be multiples of 8 elements");
   if (!aligned16(t) || !aligned16(out))

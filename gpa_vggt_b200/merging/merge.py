@@ -77,21 +77,10 @@ def build_plan(metric: torch.Tensor, w: int, h: int, sx: int, sy: int, r: int,
         a, b = kernels.metric_split(metric, src_pos, dst_pos)
         if src_pos.numel():
             node_max, node_idx = kernels.sim_argmax(a[None], b[None])
-            node_max = matcher_scores(node_max, metric.dtype)
         else:
             node_max = torch.empty(1, 0, device=dev)
             node_idx = torch.empty(1, 0, device=dev, dtype=torch.int32)
         return kernels.merge_plan(node_max[0], node_idx[0], r, dst_pos, src_pos)
-
-
-def matcher_scores(node_max: torch.Tensor, metric_dtype) -> torch.Tensor:
-    """node_max as the reference's matcher hands it to the edge ranking: in the
-    metric's dtype (fused_similarity.py:112 casts the fp32 maxima to a.dtype,
-    merge.py:13-36 keeps bf16 scores), so a bf16 metric -- the GPU run under
-    autocast -- ranks edges on bf16-rounded maxima.  Kept as fp32 values."""
-    if metric_dtype == torch.bfloat16:
-        return node_max.to(torch.bfloat16).float()
-    return node_max
 
 
 def token_merge_bipartite2d(

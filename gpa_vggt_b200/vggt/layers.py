@@ -17,7 +17,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .. import kernels
-from ..merging.merge import build_plan, draw_dst_choice, matcher_scores, projection_basis
+from ..merging.merge import build_plan, draw_dst_choice, projection_basis
 
 BF16 = torch.bfloat16
 
@@ -271,7 +271,7 @@ def merged_attention_sharded(x, q, k, v, attn: Attention) -> torch.Tensor:
     b_full = sh.gather_varlen(b, [rd[1] - rd[0] for rd, _ in ranges])
     if s1 > s0:
         nm, ni = kernels.sim_argmax(a[None], b_full[None])
-        nm, ni = matcher_scores(nm[0], metric.dtype), ni[0]
+        nm, ni = nm[0], ni[0]
     else:
         nm = torch.empty(0, device=dev)
         ni = torch.empty(0, device=dev, dtype=torch.int32)

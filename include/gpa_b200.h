@@ -163,6 +163,11 @@ GPA_API int gpa_merge_plan_noalloc(const float* node_max, const int32_t* node_id
  * (dst first, then src ordinal ascending), so the result is deterministic.
  * head_dim % 8 == 0.  If log_counts != NULL, log of the tokens behind each slot
  * (fp32 [N_m]) is also written there.
+ * The output slots are unm_len + num_dst > 0 (either part may be empty), so a
+ * caller can merge any contiguous range of a plan's unmerged slots (offset
+ * unm_src, num_dst = 0) or dst slots (offset dst_pos and seg_start, unm_len =
+ * 0): the frame-sharded path merges only the slots whose tokens it owns, with
+ * src_pos/dst_pos mapping ordinals to rows of its own row buffer.
  */
 GPA_API int gpa_merge_kv_mean(const void* t, int dtype, int heads, int n_tokens, int head_dim,
                       int64_t t_stride_h, int64_t t_stride_n, const int32_t* src_pos,

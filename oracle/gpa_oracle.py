@@ -86,22 +86,14 @@ def project_metric(x: torch.Tensor, proj: torch.Tensor, autocast_bf16: bool = Tr
     return bf16_round(y.float())
 
 
-def normalize_rows(m: torch.Tensor, bf16_metric: Optional[bool] = None) -> torch.Tensor:
+def normalize_rows(m: torch.Tensor) -> torch.Tensor:
     """metric / metric.norm(dim=-1) (merge.py:186), then the bf16 cast of
-    fused_similarity.py:90-95.
-
-    fp32 metric (the reference's CPU fp32 run): fp32 norm and division.  bf16
-    metric (its GPU run: under autocast `metric @ proj` comes out bf16): torch's
-    bf16 norm accumulates in fp32 and rounds the norm to bf16, and the bf16
-    division rounds the fp32 quotient to bf16.  bf16_metric defaults to
-    m.dtype == bf16; pass True for bf16 values held in an fp32 tensor."""
-    if bf16_metric is None:
-        bf16_metric = m.dtype == torch.bfloat16
+    fused_similarity.py:90-101.  The norm and the quotient are fp32 for a bf16
+    metric too: in the reference's GPU run under autocast `metric @ proj` comes
+    out bf16 but `norm` is on autocast's fp32 list, so the division promotes to
+    fp32 and the matcher rounds its fp32 inputs to bf16."""
     m = m.float()
-    nrm = m.norm(dim=-1, keepdim=True)
-    if bf16_metric:
-        nrm = bf16_round(nrm)
-    return bf16_round(m / nrm)
+    return bf16_round(m / m.norm(dim=-1, keepdim=True))
 
 
 # ----------------------------------------------------------------------------
@@ -288,7 +280,7 @@ def merged_attention(x, q, k, v, proj, rand_idx, ratio, w, h, num_special, scale
     mask = dst_mask(S, w, h, sx, sy, num_special, rand_idx)
     dst_pos, src_pos = split_positions(mask)
     metric = project_metric(x, proj)
-    mn = normalize_rows(metric, bf16_metric=True)
+    mn = normalize_rows(metric)
     a, b = mn[src_pos], mn[dst_pos]
     node_max, node_idx, gap = sim_argmax(a, b)
     r = int(N * ratio)

@@ -98,7 +98,7 @@ def test_metric_split_matches_oracle(dtype):
     perm = torch.randperm(2000, generator=g)
     src, dst = perm[:1500].sort().values, perm[1500:].sort().values
     a, b = kernels.metric_split(metric.to(DEV), src.int().to(DEV), dst.int().to(DEV))
-    ref = O.normalize_rows(metric)   # bf16: the norm is rounded to bf16 as torch does
+    ref = O.normalize_rows(metric)
     for got, pos in ((a, src), (b, dst)):
         d = (got.cpu().float() - ref[pos]).abs()
         ulp = ref[pos].abs() * 2 ** -7 + 1e-30

@@ -70,13 +70,16 @@ def _closure(fn):
 
 def _metric(x):
     """The normalised bf16 metric the reference's matcher sees (merge.py:180-187
-    under autocast), for the exact top-2 gaps."""
+    under autocast: a bf16 product, an fp32 norm and quotient, the matcher's
+    bf16 cast), for the exact top-2 gaps."""
     g = torch.Generator(device=DEV)
     g.manual_seed(1234)
     proj = torch.randn(x.shape[-1], 128, device=DEV, dtype=torch.float32, generator=g).to(x.dtype)
     with torch.autocast("cuda", dtype=torch.bfloat16):
         m = x[0] @ proj
-    return (m / m.norm(dim=-1, keepdim=True)).bfloat16()
+        q = m / m.norm(dim=-1, keepdim=True)
+    assert q.dtype == torch.float32
+    return q.bfloat16()
 
 
 def _top2_gap(a, b, rows):
@@ -222,3 +225,40 @@ def test_attention_keybias_matches_reference_triton_kernel(ref):
           f"max |dlse| {float((lse - lse_ref).abs().max()):.2e}")
     assert err < 1e-2
     assert float((lse - lse_ref).abs().max()) < 2e-3
+
+
+def test_forward_matches_reference_gpu_forward(ref):
+    """The whole GPA-VGGT forward at S=4 (bf16 under autocast, init_weights
+    seed 0, torch.rand frames seed 0) against the reference's own forward on
+    the same GPU with the same weights, frames and CUDA draws.  Bound: the
+    larger of 2e-2 and 1.5x the reference's own bf16 drift: its bf16 forward
+    against its fp32 forward on this GPU (fp32 runs its SDPA path: its Triton
+    attention returns bf16 for fp32 inputs, which its fp32 proj cannot take)."""
+    sys.path.insert(0, str(ROOT))
+    from gpa_vggt_b200.vggt import VGGT, init_weights
+    from vggt.models.vggt import VGGT as RefVGGT              # the reference's model
+    S = 4
+    images = torch.rand(1, S, 3, 518, 518, generator=torch.Generator().manual_seed(0)).to(DEV)
+
+    def run(model, bf16):
+        model = model.eval().to(DEV)
+        model.update_patch_dimensions(37, 37)
+        if bf16:
+            model = model.to(torch.bfloat16)
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16, enabled=bf16):
+            out = model(images)
+        return {k: out[k].float() for k in ("pose_enc", "depth", "depth_conf")}
+    import vggt.layers.attention as ref_attention             # the reference's module
+    theirs16 = run(init_weights(RefVGGT(), seed=0), True)
+    fused = ref_attention.attention_keybias
+    ref_attention.attention_keybias = None
+    try:
+        theirs32 = run(init_weights(RefVGGT(), seed=0), False)
+    finally:
+        ref_attention.attention_keybias = fused
+    ours = run(init_weights(VGGT(), seed=0), True)
+    for key in ours:
+        err = float((ours[key] - theirs16[key]).norm() / theirs16[key].norm())
+        drift = float((theirs16[key] - theirs32[key]).norm() / theirs32[key].norm())
+        print(f"{key}: ours vs reference bf16 {err:.2e}; reference bf16 vs its fp32 {drift:.2e}")
+        assert err < max(2e-2, 1.5 * drift), key
