@@ -217,6 +217,30 @@ def merge_kv(t: torch.Tensor, plan: MergePlan, mean: bool = True, out: Optional[
     return out
 
 
+def merge_kv_rows(rows: torch.Tensor, src_map: torch.Tensor, dst_map: Optional[torch.Tensor],
+                  unm_src: Optional[torch.Tensor], seg_start: Optional[torch.Tensor],
+                  seg_src: Optional[torch.Tensor], num_dst: int, out: torch.Tensor,
+                  mean: bool = True) -> torch.Tensor:
+    """Merge a contiguous range of a plan's slots from a token-major row buffer
+    rows [R, C]: the unmerged slots of unm_src (src ordinals), then num_dst dst
+    slots whose dst rows are dst_map[0..num_dst) and whose members are
+    seg_src[seg_start[j]:seg_start[j+1]] (seg_start already offset to the
+    range's first slot).  src_map / dst_map give each ordinal's row in `rows`.
+    out [n_unm + num_dst, C] receives the slots in that order (same kernel and
+    summation order as merge_kv)."""
+    require_cuda(rows, out, what="merge_kv_rows")
+    R, C = rows.shape
+    if rows.stride(1) != 1 or rows.stride(0) % 8 or out.stride(1) != 1 or out.stride(0) % 8:
+        raise ValueError("merge_kv_rows: rows and out must be row-major with 8-element-aligned rows")
+    n_unm = 0 if unm_src is None else unm_src.numel()
+    if n_unm + num_dst == 0:
+        return out
+    call("gpa_merge_kv_mean", ptr(rows), _dt(rows), 1, R, C, 0, rows.stride(0), ptr(src_map),
+         ptr(dst_map), ptr(unm_src), n_unm, ptr(seg_start), ptr(seg_src), int(num_dst), int(mean),
+         None, ptr(out), 0, out.stride(0), stream_of(rows))
+    return out
+
+
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bias: Optional[torch.Tensor],
               sm_scale: float, return_lse: bool = False, out: Optional[torch.Tensor] = None,
               status: Optional[torch.Tensor] = None, combine=None,

@@ -237,8 +237,10 @@ def _merge_draws(attn: Attention, num_imgs: int, C: int, device, dtype):
 
 def merged_attention_sharded(x, q, k, v, attn: Attention) -> torch.Tensor:
     """Merged block with the queries sharded by frame (see shard.py): every rank
-    builds the same global plan from all-gathered match results and merges the
-    all-gathered K/V; attention runs for the rank's own queries only."""
+    builds the same global plan from all-gathered match results, merges the
+    output slots of its own frames (merge_exchange) and attends with its own
+    queries against all merged keys."""
+    from .shard import merge_exchange
     sh = attn.shard
     B, Nl, C = x.shape
     H, D = attn.num_heads, attn.head_dim
@@ -248,16 +250,6 @@ def merged_attention_sharded(x, q, k, v, attn: Attention) -> torch.Tensor:
     if Nl != sh.local * P:
         raise ValueError("merged_attention_sharded: local tokens do not match the frame shard")
     dev = x.device
-    # the key/value exchange (the bulk of the bytes) starts first and overlaps
-    # the matching below; K and V travel as one [N, 2, H, D] buffer
-    if k.dtype == v.dtype:
-        kv_full, kv_work = sh.gather_async(torch.stack((k[0], v[0]), 1))
-        k_full, v_full = kv_full[:, 0], kv_full[:, 1]
-        works = (kv_work,)
-    else:   # fp32 K (unfused qk path) and bf16 V: two exchanges
-        k_full, kw = sh.gather_async(k[0])
-        v_full, vw = sh.gather_async(v[0])
-        works = (kw, vw)
     rand_idx, proj = _merge_draws(attn, S, C, dev, x.dtype)
     dst_pos, src_pos, _ = kernels.merge_roles(rand_idx, S, pw, ph, g, g, ns, False, dev)
     dpf = ns + (ph // g) * (pw // g)
@@ -279,14 +271,16 @@ def merged_attention_sharded(x, q, k, v, attn: Attention) -> torch.Tensor:
     nm_full = sh.gather_varlen(nm, src_counts)
     ni_full = sh.gather_varlen(ni, src_counts)
     plan = kernels.merge_plan(nm_full, ni_full, int(N * attn.merge_ratio), dst_pos, src_pos)
-    for w in works:
-        w.wait()
-    km = kernels.merge_kv(k_full.transpose(0, 1), plan)   # [H, N, D] (strided) views
-    vm = kernels.merge_kv(v_full.transpose(0, 1), plan)
+    # K and V travel and merge as one [tokens, 2*H*D] row buffer (V widened to
+    # K's dtype when they differ: exact, and the merged V is rounded back below)
+    kv = torch.stack((k[0], v[0].to(k.dtype)), 1).reshape(Nl, 2 * H * D)
+    merged = merge_exchange(sh, kv, plan, P, kernels).view(plan.n_out, 2, H, D)
+    km, vm = merged[:, 0].to(BF16), merged[:, 1].to(BF16)
     bias = plan.counts.log().to(BF16).float()
     out = torch.empty(1, Nl, H, D, device=dev, dtype=BF16)
-    kernels.attention(q.to(BF16).permute(0, 2, 1, 3), km.to(BF16)[None], vm.to(BF16)[None],
-                      bias[None, None], attn.scale, out=out.permute(0, 2, 1, 3))
+    kernels.attention(q.to(BF16).permute(0, 2, 1, 3), km.permute(1, 0, 2)[None],
+                      vm.permute(1, 0, 2)[None], bias[None, None], attn.scale,
+                      out=out.permute(0, 2, 1, 3))
     return out
 
 

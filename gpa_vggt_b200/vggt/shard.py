@@ -7,8 +7,10 @@ with NCCL all-gathers (one process per GPU, torch.distributed):
 
 * merged blocks: the dst metric rows (so each rank matches its own src tokens
   against all dst tokens), the (node_max, node_idx) pairs of every src token
-  (so every rank builds the identical global merge plan, top-r cut included),
-  then K and V, which every rank merges itself;
+  (so every rank builds the identical global merge plan, top-r cut included);
+  then each rank merges the output slots whose tokens sit in its own frames:
+  an all-to-all brings it the K/V rows of the members it lacks, and the merged
+  K/V of every slot is all-gathered (merge_exchange);
 * frame + shared-set blocks: the shared set only (special tokens and pooled
   summaries of every frame, 30 per frame and head);
 * plain global attention: K and V;
@@ -63,6 +65,26 @@ class FrameShard:
         work = dist.all_gather_into_tensor(out, t, group=self.kv_group, async_op=True)
         return out, work
 
+    def all_to_all(self, out: torch.Tensor, inp: torch.Tensor, out_splits: List[int],
+                   in_splits: List[int]) -> torch.Tensor:
+        """Rows of inp go to the ranks in order (in_splits[i] to rank i); out
+        receives out_splits[i] rows from rank i, in rank order."""
+        dist.all_to_all_single(out, inp.contiguous(), out_splits, in_splits, group=self.group)
+        return out
+
+    def gather_varlen2(self, a: torch.Tensor, b: torch.Tensor, counts_a: Sequence[int],
+                       counts_b: Sequence[int]):
+        """Two variable-length all-gathers along dim 0 in one collective: rank i
+        holds counts_a[i] rows of a and counts_b[i] rows of b (same row shape)."""
+        ma, mb = max(counts_a), max(counts_b)
+        pad = torch.zeros((ma + mb,) + tuple(a.shape[1:]), device=a.device, dtype=a.dtype)
+        pad[: a.shape[0]] = a
+        pad[ma: ma + b.shape[0]] = b
+        full = self.gather(pad).view((self.world, ma + mb) + tuple(a.shape[1:]))
+        ga = torch.cat([full[i, : counts_a[i]] for i in range(self.world)], 0)
+        gb = torch.cat([full[i, ma: ma + counts_b[i]] for i in range(self.world)], 0)
+        return ga, gb
+
     def gather_varlen(self, t: torch.Tensor, counts: Sequence[int]) -> torch.Tensor:
         """All-gather along dim 0 when rank i holds counts[i] rows."""
         m = max(counts)
@@ -89,3 +111,60 @@ class FrameShard:
                 s += ns
             out.append(((d0, d), (s0, s)))
         return out
+
+
+def merge_exchange(sh: FrameShard, rows: torch.Tensor, plan, tokens_per_frame: int,
+                   kernels) -> torch.Tensor:
+    """Merged rows of every output slot of `plan` (identical on every rank),
+    from this rank's token rows [local_frames * P, C].
+
+    Each output slot belongs to the rank whose frames hold its token (the
+    unmerged src token, or the dst token); since ordinals are frame-major, a
+    rank's slots are one contiguous range of unmerged slots and one of dst
+    slots.  The members of a rank's dst slots that sit in other ranks' frames
+    come over one all-to-all; the rank merges its slots with the same kernel
+    and summation order as one GPU would (bit-identical results), and one
+    all-gather gives every rank all merged rows in slot order.  Returns
+    [N_m, C] in rows' dtype."""
+    world, rank = sh.world, sh.rank
+    dev = rows.device
+    LP = sh.local * tokens_per_frame
+    base = rank * LP
+    src_pos, dst_pos = plan.src_pos.long(), plan.dst_pos.long()
+    seg = plan.seg_start.long()
+    unm_owner = torch.div(src_pos[plan.unm_src.long()], LP, rounding_mode="floor")
+    dst_owner = torch.div(dst_pos, LP, rounding_mode="floor")
+    mem_dst = torch.repeat_interleave(torch.arange(plan.num_dst, device=dev), seg[1:] - seg[:-1])
+    mem_src = plan.seg_src.long()
+    mem_owner = dst_owner[mem_dst]
+    mem_rank = torch.div(src_pos[mem_src], LP, rounding_mode="floor")
+    move = mem_owner != mem_rank
+    # one small device-to-host read: slot counts per rank and the row matrix
+    cnt = torch.cat([torch.bincount(unm_owner, minlength=world), torch.bincount(dst_owner, minlength=world),
+                     torch.bincount((mem_rank * world + mem_owner)[move], minlength=world * world)]).cpu()
+    unm_cnt, dst_cnt = cnt[:world].tolist(), cnt[world:2 * world].tolist()
+    mat = cnt[2 * world:].view(world, world)
+    # send: this rank's member rows that other ranks' slots need, by owner rank
+    mine = (move & (mem_rank == rank)).nonzero().reshape(-1)
+    send_m = mine[torch.sort(mem_owner[mine], stable=True).indices]
+    send = rows[src_pos[mem_src[send_m]] - base]
+    recv = torch.empty((int(mat[:, rank].sum()),) + tuple(rows.shape[1:]), device=dev, dtype=rows.dtype)
+    sh.all_to_all(recv, send, mat[:, rank].tolist(), mat[rank].tolist())
+    # receive: the members of this rank's slots from elsewhere, by source rank
+    theirs = (move & (mem_owner == rank)).nonzero().reshape(-1)
+    recv_m = theirs[torch.sort(mem_rank[theirs], stable=True).indices]
+    buf = torch.cat([rows, recv]) if recv.shape[0] else rows
+    src_map = (src_pos - base).to(torch.int32)
+    src_map[mem_src[recv_m]] = torch.arange(LP, LP + recv_m.numel(), device=dev, dtype=torch.int32)
+    dst_map = (dst_pos - base).to(torch.int32)
+    u0, e0 = sum(unm_cnt[:rank]), sum(dst_cnt[:rank])
+    nu, nd = unm_cnt[rank], dst_cnt[rank]
+    out = torch.empty((nu + nd,) + tuple(rows.shape[1:]), device=dev, dtype=rows.dtype)
+    if nu:
+        kernels.merge_kv_rows(buf, src_map, None, plan.unm_src[u0:u0 + nu], None, None, 0, out[:nu])
+    if nd:
+        kernels.merge_kv_rows(buf, src_map, dst_map[e0:], None, plan.seg_start[e0:], plan.seg_src,
+                              nd, out[nu:])
+    unm_all, dst_all = sh.gather_varlen2(out[:nu], out[nu:], unm_cnt, dst_cnt)
+    return torch.cat([unm_all, dst_all])
+

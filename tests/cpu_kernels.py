@@ -53,10 +53,34 @@ def sim_argmax(a, b, status=None):
 
 
 def merge_plan(node_max, node_idx, r, dst_pos, src_pos):
+    """The oracle's plan, also in the CSR form of kernels.MergePlan."""
+    from gpa_vggt_b200.kernels import MergePlan
     ns, nd = src_pos.numel(), dst_pos.numel()
     plan = O.merge_plan(node_max.double(), node_idx.long(), r, nd)
-    return SimpleNamespace(oracle=plan, dst=dst_pos.long(), src=src_pos.long(),
-                           counts=plan.counts.float(), n_out=plan.unm_len + nd)
+    merged = torch.nonzero(plan.merged).reshape(-1)
+    ni = node_idx.long()
+    seg_src = merged[torch.sort(ni[merged], stable=True).indices]
+    seg_start = torch.zeros(nd + 1, dtype=torch.long)
+    seg_start[1:] = torch.cumsum(torch.bincount(ni[merged], minlength=nd), 0)
+    mp = MergePlan(ns, nd, int(merged.numel()), dst_pos, src_pos, plan.unm_src.int(), seg_start.int(),
+                   seg_src.int(), plan.counts.float(), node_max, node_idx)
+    mp.oracle, mp.dst, mp.src = plan, dst_pos.long(), src_pos.long()
+    return mp
+
+
+def merge_kv_rows(rows, src_map, dst_map, unm_src, seg_start, seg_src, num_dst, out, mean=True):
+    r = rows.double()
+    res = []
+    for u in ([] if unm_src is None else unm_src.tolist()):
+        res.append(r[int(src_map[u])])
+    for j in range(num_dst):
+        a0, a1 = int(seg_start[j]), int(seg_start[j + 1])
+        acc = r[int(dst_map[j])].clone()
+        for m in seg_src[a0:a1].tolist():
+            acc = acc + r[int(src_map[m])]
+        res.append(acc / (1 + a1 - a0) if mean else acc)
+    out.copy_(torch.stack(res).to(out.dtype))
+    return out
 
 
 def merge_kv(t, plan, mean=True, out=None, log_counts=None):
@@ -96,7 +120,7 @@ def install(setattr_fn, fp32=True):
     from gpa_vggt_b200 import kernels
     from gpa_vggt_b200.vggt import layers
     for name in ("attention", "merge_roles", "metric_split", "sim_argmax", "merge_plan", "merge_kv",
-                 "frame_pool", "lse_combine"):
+                 "merge_kv_rows", "frame_pool", "lse_combine"):
         setattr_fn(kernels, name, globals()[name])
     setattr_fn(layers, "build_plan", build_plan)
     if fp32:

@@ -145,3 +145,50 @@ def test_gather_async_on_the_kv_communicator(tmp_path):
         assert got["k"][:3].eq(0).all() and got["k"][3:].eq(1).all()
         assert got["v"][:3].float().eq(10).all() and got["v"][3:].float().eq(11).all()
         assert torch.equal(got["kv"][:, 0], got["k"]) and torch.equal(got["kv"][:, 1], got["v"].float())
+
+
+def _exchange_worker(rank, world, port, tmpdir):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import cpu_kernels
+    from gpa_vggt_b200.vggt.shard import FrameShard, merge_exchange
+    sh = FrameShard(4)
+    plan, rows, P = _exchange_case()
+    mine = rows[sh.f0 * P:sh.f1 * P]
+    merged = merge_exchange(sh, mine, plan, P, cpu_kernels)
+    torch.save(merged, os.path.join(tmpdir, f"x{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _exchange_case(ratio=0.6):
+    """A 4-frame 9x9 split, random matches across all frames (many member rows
+    sit in other frames than their dst), rows of 16 features."""
+    import cpu_kernels
+    g = torch.Generator().manual_seed(21)
+    P = 9 * 9 + 5
+    rand = torch.randint(4, size=(3, 4, 4), generator=g)
+    dst, src, _ = cpu_kernels.merge_roles(rand, 4, 9, 9, 2, 2, 5, False, "cpu")
+    nm = torch.rand(src.numel(), generator=g)
+    ni = torch.randint(0, dst.numel(), (src.numel(),), generator=g)
+    plan = cpu_kernels.merge_plan(nm, ni, int(4 * P * ratio), dst, src)
+    rows = torch.randn(4 * P, 16, generator=g)
+    return plan, rows, P
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_merge_exchange_matches_single_merge(tmp_path, world):
+    """Every rank gets the merged rows of every slot, equal to merging all
+    tokens on one rank (same plan, same summation order)."""
+    import cpu_kernels
+    plan, rows, P = _exchange_case()
+    want = cpu_kernels.merge_kv(rows[None], plan)[0]          # one "head" of 16 features
+    mp.start_processes(_exchange_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       start_method="spawn")
+    for r in range(world):
+        got = torch.load(tmp_path / f"x{r}.pt")
+        assert got.shape == want.shape
+        assert torch.allclose(got, want, atol=1e-6, rtol=1e-6)
