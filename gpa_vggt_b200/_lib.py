@@ -37,6 +37,7 @@ SIGNATURES = {
     "gpa_merge_counts": (_c_int, [_c_int] * 7 + [ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
     "gpa_merge_roles": (_c_int, [_vp] + [_c_int] * 7 + [_vp, _vp, _vp, _vp]),
     "gpa_metric_split": (_c_int, [_vp, _c_int, _c_i64, _c_int, _vp, _c_int, _vp, _c_int, _vp, _vp, _vp]),
+    "gpa_proj_norm_split": (_c_int, [_vp, _c_i64, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _vp]),
     "gpa_merge_plan_workspace_bytes": (_c_i64, [_c_int, _c_int]),
     "gpa_merge_plan": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _c_i64, _vp]),
     "gpa_merge_plan_noalloc": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp]),

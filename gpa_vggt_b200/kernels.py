@@ -158,6 +158,30 @@ def metric_split(metric: torch.Tensor, src_pos, dst_pos):
     return a, b
 
 
+def proj_norm_split(x: torch.Tensor, proj_t: torch.Tensor, slot: torch.Tensor, num_src: int,
+                    num_dst: int, status: Optional[torch.Tensor] = None):
+    """bf16 a [num_src, 128] (src rows) and b [num_dst, 128] (dst rows) of
+    normalise(bf16(x @ proj)) for x [T, K] bf16 and proj_t = proj^T [128, K]
+    bf16, routed by the role slot map [T] of merge_roles (one tcgen05 kernel)."""
+    require_cuda(x, proj_t, slot, what="proj_norm_split")
+    if x.dtype != BF16 or proj_t.dtype != BF16 or slot.dtype != torch.int32:
+        raise TypeError("proj_norm_split: bf16 x and proj_t, int32 slot")
+    if x.stride(-1) != 1 or x.stride(0) % 8 or not aligned(x):
+        x = x.contiguous()
+    proj_t = proj_t.contiguous()
+    T, K = x.shape
+    if tuple(proj_t.shape) != (128, K) or slot.numel() != T:
+        raise ValueError("proj_norm_split: proj_t must be [128, K] and slot [T]")
+    a = torch.empty(num_src, 128, device=x.device, dtype=BF16)
+    b = torch.empty(num_dst, 128, device=x.device, dtype=BF16)
+    status, own = _status_word(status, x.device)
+    call("gpa_proj_norm_split", ptr(x), x.stride(0), T, K, ptr(proj_t), ptr(slot.contiguous()),
+         ptr(a), ptr(b), ptr(status), stream_of(x))
+    if own:
+        _check_status(status, "gpa_proj_norm_split")
+    return a, b
+
+
 @dataclass
 class MergePlan:
     """Device arrays describing one bipartite merge (B == 1)."""

@@ -40,6 +40,27 @@ def projection_basis(c: int, metric_dim: int, device, dtype) -> torch.Tensor:
     return p
 
 
+_proj_t_cache = {}
+
+
+def projection_basis_t(c: int, metric_dim: int, device) -> torch.Tensor:
+    """proj^T [metric_dim, c] in bf16, contiguous (the fused projection kernel's
+    K-major operand), drawn as projection_basis draws proj."""
+    key = (str(device), c, metric_dim)
+    p = _proj_t_cache.get(key)
+    if p is None:
+        p = projection_basis(c, metric_dim, device, torch.bfloat16).t().contiguous()
+        _proj_t_cache[key] = p
+    return p
+
+
+def fused_metric_ok(metric: torch.Tensor, metric_dim: int) -> bool:
+    """Whether the one-kernel projection + normalisation applies: a bf16 metric
+    (the autocast run) projected to 128 dims from a width that is a multiple of 64."""
+    C = metric.shape[-1]
+    return metric.dtype == torch.bfloat16 and metric_dim == 128 and C > 128 and C % 64 == 0
+
+
 def draw_dst_choice(num_imgs: int, w: int, h: int, sx: int, sy: int, device,
                     generator: Optional[torch.Generator]) -> Optional[torch.Tensor]:
     """The per-window dst pick of merge.py:121-126 (same RNG call)."""
@@ -67,14 +88,20 @@ def build_plan(metric: torch.Tensor, w: int, h: int, sx: int, sy: int, r: int,
     dev = metric.device
     if not no_rand and rand_idx is None:
         rand_idx = draw_dst_choice(num_imgs, w, h, sx, sy, dev, generator)
-    dst_pos, src_pos, _ = kernels.merge_roles(None if no_rand else rand_idx, num_imgs, w, h,
-                                              sx, sy, num_special, no_rand, dev)
+    dst_pos, src_pos, slot = kernels.merge_roles(None if no_rand else rand_idx, num_imgs, w, h,
+                                                 sx, sy, num_special, no_rand, dev)
     with torch.no_grad():
-        if metric_dim and metric_dim < C:
-            if proj is None:
-                proj = projection_basis(C, metric_dim, dev, metric.dtype)
-            metric = metric @ proj.to(metric.dtype)
-        a, b = kernels.metric_split(metric, src_pos, dst_pos)
+        if fused_metric_ok(metric, metric_dim):
+            # projection, bf16 rounding, fp32 normalisation and split in one kernel
+            proj_t = (projection_basis_t(C, metric_dim, dev) if proj is None
+                      else proj.to(torch.bfloat16).t().contiguous())
+            a, b = kernels.proj_norm_split(metric, proj_t, slot, src_pos.numel(), dst_pos.numel())
+        else:
+            if metric_dim and metric_dim < C:
+                if proj is None:
+                    proj = projection_basis(C, metric_dim, dev, metric.dtype)
+                metric = metric @ proj.to(metric.dtype)
+            a, b = kernels.metric_split(metric, src_pos, dst_pos)
         if src_pos.numel():
             node_max, node_idx = kernels.sim_argmax(a[None], b[None])
         else:

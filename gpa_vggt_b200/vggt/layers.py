@@ -17,7 +17,8 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .. import kernels
-from ..merging.merge import build_plan, draw_dst_choice, projection_basis
+from ..merging.merge import (build_plan, draw_dst_choice, fused_metric_ok, projection_basis,
+                             projection_basis_t)
 
 BF16 = torch.bfloat16
 
@@ -251,15 +252,23 @@ def merged_attention_sharded(x, q, k, v, attn: Attention) -> torch.Tensor:
         raise ValueError("merged_attention_sharded: local tokens do not match the frame shard")
     dev = x.device
     rand_idx, proj = _merge_draws(attn, S, C, dev, x.dtype)
-    dst_pos, src_pos, _ = kernels.merge_roles(rand_idx, S, pw, ph, g, g, ns, False, dev)
+    dst_pos, src_pos, slot = kernels.merge_roles(rand_idx, S, pw, ph, g, g, ns, False, dev)
     dpf = ns + (ph // g) * (pw // g)
     ranges = sh.role_ranges(P, dpf)
     (d0, d1), (s0, s1) = ranges[sh.rank]
     base = sh.f0 * P
     metric = x[0]
-    if attn.merge_metric_dim and attn.merge_metric_dim < C:
-        metric = metric @ proj.to(metric.dtype)
-    a, b = kernels.metric_split(metric, src_pos[s0:s1] - base, dst_pos[d0:d1] - base)
+    if fused_metric_ok(metric, attn.merge_metric_dim):
+        # this rank's rows, with the role map renumbered to its own ordinals
+        sl = slot[base:base + Nl]
+        sl = torch.where(sl >= 0, sl - d0, sl + s0).to(torch.int32)
+        proj_t = (projection_basis_t(C, attn.merge_metric_dim, dev) if attn.rng_override is None
+                  else proj.to(BF16).t().contiguous())
+        a, b = kernels.proj_norm_split(metric, proj_t, sl, s1 - s0, d1 - d0)
+    else:
+        if attn.merge_metric_dim and attn.merge_metric_dim < C:
+            metric = metric @ proj.to(metric.dtype)
+        a, b = kernels.metric_split(metric, src_pos[s0:s1] - base, dst_pos[d0:d1] - base)
     b_full = sh.gather_varlen(b, [rd[1] - rd[0] for rd, _ in ranges])
     if s1 > s0:
         nm, ni = kernels.sim_argmax(a[None], b_full[None])

@@ -116,6 +116,21 @@ GPA_API int gpa_metric_split(const void* metric, int dtype, int64_t metric_strid
                      void* stream);
 
 /*
+ * Matching metric in one pass (replaces merging/merge.py:180-187, the
+ * `metric @ proj`, normalisation and split): for each of the `rows` rows of x
+ * (bf16, row stride x_stride >= k, k % 64 == 0), m = bf16(x_row @ proj) with
+ * proj_t = proj^T [128, k] bf16 contiguous (fp32 accumulation, the product
+ * rounded to bf16 as the reference's autocast GEMM returns it), then
+ * bf16(m / ||m||) with the norm and quotient in fp32 (the reference's
+ * `metric.norm()` runs in fp32 under autocast).  The 128-wide result goes to
+ * row slot[i] of b when slot[i] >= 0 (a dst token) and to row -slot[i]-1 of a
+ * otherwise (a src token): the slot map of gpa_merge_roles.  a, b: [*, 128]
+ * bf16 contiguous.  tcgen05 kernel; status as for the other pipelined kernels.
+ */
+GPA_API int gpa_proj_norm_split(const void* x, int64_t x_stride, int rows, int k, const void* proj_t,
+                                const int32_t* slot, void* a, void* b, int* status, void* stream);
+
+/*
  * Merge plan (replaces merging/merge.py:189-217).  Given node_max/node_idx of
  * the num_src src tokens, the r = min(r, num_src) src tokens with the largest
  * node_max are merged into their matched dst; ties at the cut are broken by
