@@ -17,6 +17,7 @@ Representation differences (results are the same up to slot order):
   * at the top-r cut, ties in node_max go to the lower src ordinal.
   * group sums are fp32 in a fixed order (deterministic).
 """
+import os
 from typing import Callable, Optional
 
 import torch
@@ -54,11 +55,20 @@ def projection_basis_t(c: int, metric_dim: int, device) -> torch.Tensor:
     return p
 
 
+# The one-kernel projection sums the product in its own order, so about one
+# metric element in 10^5 rounds to the other bf16 neighbour than the
+# reference's cuBLAS product; a src row whose two best dst tokens are closer
+# than about 5e-4 can then match the other one.  GPA_FUSED_METRIC=0 keeps
+# torch's GEMM for the product (bit-identical matcher inputs).
+FUSED_METRIC = os.environ.get("GPA_FUSED_METRIC", "1") == "1"
+
+
 def fused_metric_ok(metric: torch.Tensor, metric_dim: int) -> bool:
     """Whether the one-kernel projection + normalisation applies: a bf16 metric
     (the autocast run) projected to 128 dims from a width that is a multiple of 64."""
     C = metric.shape[-1]
-    return metric.dtype == torch.bfloat16 and metric_dim == 128 and C > 128 and C % 64 == 0
+    return (FUSED_METRIC and metric.dtype == torch.bfloat16 and metric_dim == 128 and C > 128
+            and C % 64 == 0)
 
 
 def draw_dst_choice(num_imgs: int, w: int, h: int, sx: int, sy: int, device,

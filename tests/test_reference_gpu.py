@@ -109,8 +109,17 @@ def _maps(mr, mo, N):
     return cv, plan, ref_dst_of, ours_dst_of
 
 
+@pytest.mark.parametrize("fused", [False, True])
 @pytest.mark.parametrize("S,ratio", [(10, 0.98), (10, 0.2), (200, 0.98), (200, 0.2)])
-def test_merge_plan_matches_reference_gpu_path(ref, S, ratio):
+def test_merge_plan_matches_reference_gpu_path(ref, S, ratio, fused, monkeypatch):
+    """fused=False: the metric product through torch's GEMM, as the reference
+    computes it: bit-exact except rows whose exact top-2 gap is below 1e-6.
+    fused=True: the one-kernel projection (gpa_proj_norm_split), whose own
+    summation order moves about one metric element in 10^5 to the other bf16
+    neighbour: rows may also differ where the gap is below 5e-4, at most one
+    row in 10^4."""
+    from gpa_vggt_b200.merging import merge as M
+    monkeypatch.setattr(M, "FUSED_METRIC", fused)
     ref_merge, _ = ref
     N = S * P_TOK
     x = torch.randn(1, N, 1024, device=DEV, generator=_gen(S)).bfloat16()
@@ -146,7 +155,11 @@ def test_merge_plan_matches_reference_gpu_path(ref, S, ratio):
     gaps = _top2_gap(a, b, bad_rows) if bad_rows.numel() else torch.zeros(0, device=DEV)
     print(f"S={S} ratio={ratio}: {int(diff.sum())} of {int(both.sum())} merged rows matched "
           f"differently; largest top-2 gap among them {float(gaps.max()) if gaps.numel() else 0:.2e}")
-    assert int((gaps >= 1e-6).sum()) == 0
+    if fused:
+        assert int((gaps >= 5e-4).sum()) == 0
+        assert int(diff.sum()) <= 1e-4 * int(both.sum()) + 1
+    else:
+        assert int((gaps >= 1e-6).sum()) == 0
     # counts keyed by dst position, where no differing src is involved
     ref_size = mr.size.reshape(-1)
     unm_len = ref_size.numel() - b_idx.numel()
