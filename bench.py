@@ -183,7 +183,7 @@ def merged_block(x, qkv, ratio, out=None):
 # ----------------------------------------------------------------------------
 # CPU baseline: the reference's own CPU path on the host cores
 # ----------------------------------------------------------------------------
-def cpu_reference(S, vanilla=False, reps=1):
+def cpu_reference(S, vanilla=False, reps=3):
     """(ms per forward, kind, sample note, extrapolated) of the reference's CPU
     forward at S frames (oracle/reference_runs.py): the reference's own modules
     from baseline/_ref when installed (kind "reference"), else the port.  At
@@ -196,11 +196,12 @@ def cpu_reference(S, vanilla=False, reps=1):
         return RR.port_forward_ms(S, vanilla), "port", RR.port_sample_note(S, vanilla), True
     if S <= 10:
         model = RR.build_cpu_model(vanilla)
+        RR.forward_ms(model, S)            # warm-up
         ms = statistics.median(RR.forward_ms(model, S) for _ in range(reps))
         return ms, "reference", (f"the reference's whole fp32 forward at S={S} (baseline/_ref, "
                                  f"aggregator + camera + DPT heads)"), False
     comp = RR.Composer(S, vanilla)
-    ms = statistics.median(comp.compose_ms(comp.parts(reps=1)) for _ in range(reps))
+    ms = statistics.median(comp.compose_ms(comp.parts(reps=2)) for _ in range(reps))
     return ms, "reference", RR.composed_sample_note(S, vanilla), True
 
 
@@ -262,7 +263,7 @@ def main():
             sample = f"the reference's whole fp32 forward at S={S} (baseline/_ref)"
         elif have:
             comp = RR.Composer(S, args.vanilla)
-            one = lambda: comp.compose_ms(comp.parts(reps=1))  # noqa: E731
+            one = lambda: comp.compose_ms(comp.parts(reps=2))  # noqa: E731
             sample = RR.composed_sample_note(S, args.vanilla)
         else:
             one = lambda: RR.port_forward_ms(S, args.vanilla)  # noqa: E731

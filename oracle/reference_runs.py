@@ -165,9 +165,16 @@ class Composer:
         self.dpt = _init(R["DPTHead"](dim_in=2048, output_dim=2, activation="exp",
                                       conf_activation="expp1"), 0).eval()
         self.cam = _init(R["CameraHead"](dim_in=2048), 0).eval()
+        self.warm = False
 
     def parts(self, reps: int = 3) -> dict:
-        """Seconds per piece (medians of `reps` runs of the small pieces)."""
+        """Seconds per piece: the median of `reps` runs of each piece (the
+        first call of a Composer runs every piece once untimed: TorchScript
+        compiles the reference's matcher on its first call, and first
+        allocations are slow)."""
+        if not self.warm:
+            self.warm = True
+            self.parts(reps=1)
         R, S, N = self.R, self.S, self.N
         p = {}
         self.reps = reps
@@ -181,7 +188,7 @@ class Composer:
                 rq = 128
                 q = self.q1[:, :, :rq]
                 kk = self.k.to(torch.float32)
-                p["global_attn_per_block"] = _med(lambda: F.scaled_dot_product_attention(q, kk, kk), 1) * N / rq
+                p["global_attn_per_block"] = _med(lambda: F.scaled_dot_product_attention(q, kk, kk), reps) * N / rq
             else:
                 # early blocks, CPU path: own patches + every frame's shared set in
                 # one SDPA with the +log size bias (attention.py:178-206), per frame
@@ -193,9 +200,9 @@ class Composer:
             # heads: DPT on one frame (8-frame chunks, dpt_head.py:150-213), camera on S frames
             taps = [torch.randn(1, 1, P_TOK, 2048, generator=self.g)] * 24
             img1 = torch.rand(1, 1, 3, 518, 518, generator=self.g)
-            p["dpt_per_frame"] = _med(lambda: self.dpt(taps, images=img1, patch_start_idx=5), 1)
+            p["dpt_per_frame"] = _med(lambda: self.dpt(taps, images=img1, patch_start_idx=5), reps)
             cam_taps = [torch.randn(1, S, P_TOK, 2048, generator=self.g)] * 24
-            p["camera"] = _med(lambda: self.cam(cam_taps), 1)
+            p["camera"] = _med(lambda: self.cam(cam_taps), reps)
         return p
 
     def _merged(self) -> dict:
@@ -222,17 +229,18 @@ class Composer:
             p["merge_no_matcher"] = time.perf_counter() - t0
         finally:
             merge.fast_similarity_chunks = stock
+        reps = self.reps
         rs = min(1000, self.ns)
         a, bT = captured["a"][:, :rs].contiguous(), captured["bT"]
-        p["matcher"] = _med(lambda: stock(a, bT, rs), 1) * self.ns / rs
-        p["merge_heads_kv"] = _med(lambda: (m.heads(self.k), m.heads(self.v)), 1)
-        rq = 64
+        p["matcher"] = _med(lambda: stock(a, bT, rs), reps) * self.ns / rs
+        p["merge_heads_kv"] = _med(lambda: (m.heads(self.k), m.heads(self.v)), reps)
+        rq = 128
         q = self.q1[:, :, :rq]
         for name, ratio in (("attn_0.98", 0.98), ("attn_0.2", 0.2)):
             nm = merged_len(S, ratio)
             kk, vv = self.k[:, :, :nm], self.v[:, :, :nm]
             bias = torch.rand(1, 16, 1, nm, generator=self.g)
-            p[name] = _med(lambda: F.scaled_dot_product_attention(q, kk, vv, attn_mask=bias), 1) * N / rq
+            p[name] = _med(lambda: F.scaled_dot_product_attention(q, kk, vv, attn_mask=bias), reps) * N / rq
         return p
 
     def compose_ms(self, p: dict) -> float:
@@ -254,7 +262,7 @@ def composed_sample_note(S, vanilla):
             f"CPU pieces (baseline/_ref, fp32, all host threads): a block on one frame's tokens, "
             f"own-frame SDPA, the early blocks' SDPA with the shared set per frame, "
             f"token_merge_bipartite2d without its matcher at full size, fast_similarity_chunks on "
-            f"1,000 src rows, merge.heads of K and V at full size, the masked SDPA on 64 query "
+            f"1,000 src rows, merge.heads of K and V at full size, the masked SDPA on 128 query "
             f"rows, the DPT head on one frame, the camera head on S frames; scaled by rows/frames "
             f"and composed by the schedule ({SCHEDULE}): an extrapolation")
 
