@@ -43,7 +43,17 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 P_TOK = 37 * 37 + 5  # tokens per frame
-ATTN_TRAFFIC_RATIO = 350.9 / 341.0  # measured DRAM bytes / algorithmic bytes of attn_kernel
+# Measured DRAM bytes (ncu dram__bytes_read.sum + dram__bytes_write.sum of one
+# launch) over the algorithmic q/k/v/o bytes of attn_kernel, S=200, 16 heads:
+# 274,800 x 66,845 keys: 1.384 GB / 1.400 GB; 274,800 x 219,840 keys:
+# 4.847 GB / 2.026 GB (a head's 56 MB of K/V no longer stays in L2 between the
+# waves of its query tiles).  Launches up to 66,845 keys use the first ratio.
+ATTN_TRAFFIC_RATIO_SMALL = 1.384 / 1.400
+ATTN_TRAFFIC_RATIO_LARGE = 4.847 / 2.026
+
+
+def attn_traffic(nbytes, n_keys):
+    return nbytes * (ATTN_TRAFFIC_RATIO_LARGE if n_keys > 100_000 else ATTN_TRAFFIC_RATIO_SMALL)
 METRIC = "GPA-VGGT fwd latency (ms) & frames/s at S=200, 1/2/4/8 B200; % roofline"
 
 
@@ -141,10 +151,13 @@ def build_model(dev, vanilla=False):
 
 def forward(model, images):
     import torch
+    from gpa_vggt_b200.nvtx import nvtx
     with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
         taps, psi = model.aggregator(images)
-        pose = model.camera_head(taps, shard=model.aggregator.shard)[-1]
-        depth, conf = model.depth_head(taps, images=images, patch_start_idx=psi)
+        with nvtx("camera_head"):
+            pose = model.camera_head(taps, shard=model.aggregator.shard)[-1]
+        with nvtx("depth_head"):
+            depth, conf = model.depth_head(taps, images=images, patch_start_idx=psi)
     return pose, depth, conf
 
 
@@ -343,11 +356,21 @@ def main():
         barrier()
         torch.cuda.profiler.stop()
     launches = _lib.launch_count() - l0
+    from gpa_vggt_b200 import nvtx as _nv
+    if _nv.TIMING:   # per-range device ms of the timed steps, grouped by kind
+        bt = _nv.block_times()
+        kinds = {}
+        for name, v in bt.items():
+            k = ("global_" + name.split("_", 3)[-1]) if name.startswith("global_block") else (
+                "frame_block" if name.startswith("frame_block") else name)
+            kinds[k] = kinds.get(k, 0.0) + v / args.steps
+        print(json.dumps({"rank": rank, "block_ms_per_step": kinds}), file=sys.stderr, flush=True)
     timing, kernels.ATTN_TIMING = kernels.ATTN_TIMING, None
     ms = start.elapsed_time(stop) / args.steps
     attn_ms = sum(rec[0].elapsed_time(rec[1]) for rec in timing) / args.steps
     attn_flops = sum(rec[2] for rec in timing) / args.steps
     attn_bytes = sum(rec[3] for rec in timing) / args.steps
+    attn_traffic_bytes = sum(attn_traffic(rec[3], rec[4]) for rec in timing) / args.steps
     n_attn = len(timing) // args.steps
     if world > 1:
         t = torch.tensor([ms, attn_ms], device=dev)
@@ -418,10 +441,9 @@ def main():
             "frac_of_burst": achieved / pk["bf16"], "flops_per_step": attn_flops,
             "launches_per_step": n_attn, "ms_per_step": attn_ms,
             "share_of_step": attn_ms / ms,
-            # DRAM bytes per step: the algorithmic q/k/v/o bytes of this step's launches
-            # times the measured ratio dram__bytes_read+write / algorithmic = 1.03 of
-            # the ncu capture in profiles/attn_kernel_q16384_k66845.md (K/V read once)
-            "traffic": ATTN_TRAFFIC_RATIO * attn_bytes, "traffic_unit": "bytes per step",
+            # DRAM bytes per step: each launch's algorithmic q/k/v/o bytes times the
+            # ncu-measured DRAM/algorithmic ratio of its shape (attn_traffic)
+            "traffic": attn_traffic_bytes, "traffic_unit": "bytes per step",
             "algorithmic_bytes_per_step": attn_bytes}
     line = dict(base, value=ms, ms_per_step=ms, gpu_launches=launches, roofline=roof, e2e=e2e,
                 clocks=clk.summary())

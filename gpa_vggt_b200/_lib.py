@@ -57,6 +57,7 @@ SIGNATURES = {
                                             _c_i64, _vp, _c_i64, _c_i64, _c_int, _c_int, _c_int, _vp,
                                             _c_i64, _c_i64, _c_i64, _vp]),
     "gpa_gelu_bf16": (_c_int, [_vp, _c_i64, _vp, _vp]),
+    "gpa_bias_act_bf16": (_c_int, [_vp, _vp, _vp, _c_i64, _c_int, _c_int, _vp, _vp]),
     "gpa_residual_scale_bf16": (_c_int, [_vp, _c_i64, _vp, _c_i64, _vp, _c_int, _c_int, _vp, _c_i64, _vp]),
     "gpa_qk_norm_rope": (_c_int, [_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _vp, _vp, _vp,
                                   _vp, _c_int, _c_f32, _vp, _vp, _vp, _c_int, _vp, _vp, _c_i64, _vp]),

@@ -128,3 +128,67 @@ extern "C" int gpa_upsample_bilinear_bf16(const void* x, int x_dtype, int n, int
         (__nv_bfloat16*)out, out_sn, out_sh, out_sw, out_h, out_w, rh, rw, total);
   return check_launch("gpa_upsample_bilinear_bf16");
 }
+
+// ---------------------------------------------------------------------------
+// Convolution bias, ReLU and residual of the DPT head's convolutions, in one
+// pass over a channels-last bf16 map (replaces the bias add torch issues after
+// each cuDNN convolution, the ReLU of ResidualConvUnit and its skip add;
+// heads/dpt_head.py ResidualConvUnit, FeatureFusionBlock):
+//   t   = bf16(y + bias[c])            the conv's bias add (bf16 tensors, fp32 math)
+//   t   = relu(t)                      when relu != 0
+//   out = bf16(t + res)                when res != NULL (the residual add)
+// Each step rounds as the torch op it replaces, so the result is bit-exact.
+// y, res, out: [N, H, W, C] contiguous bf16 (channels-last), C % 8 == 0; out
+// may be y.  One thread per 8 channels of a pixel.
+// ---------------------------------------------------------------------------
+namespace gpa {
+namespace dpt {
+__global__ void __launch_bounds__(256) bias_act_kernel(const __nv_bfloat16* __restrict__ y,
+                                                       const __nv_bfloat16* __restrict__ bias,
+                                                       const __nv_bfloat16* __restrict__ res, int c,
+                                                       int64_t groups, int relu, __nv_bfloat16* out) {
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= groups) return;
+  const int c0 = (int)((g * 8) % c);
+  float v[8], b[8];
+  load8(y + g * 8, v);
+  load8(bias + c0, b);
+  float r[8];
+  if (res) load8(res + g * 8, r);
+  uint4 pk;
+  __nv_bfloat162* e = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    float t0 = __bfloat162float(__float2bfloat16_rn(v[2 * k] + b[2 * k]));
+    float t1 = __bfloat162float(__float2bfloat16_rn(v[2 * k + 1] + b[2 * k + 1]));
+    if (relu) {
+      t0 = fmaxf(t0, 0.0f);
+      t1 = fmaxf(t1, 0.0f);
+    }
+    if (res) {
+      t0 += r[2 * k];
+      t1 += r[2 * k + 1];
+    }
+    e[k] = __floats2bfloat162_rn(t0, t1);
+  }
+  *reinterpret_cast<uint4*>(out + g * 8) = pk;
+}
+}  // namespace dpt
+}  // namespace gpa
+
+extern "C" int gpa_bias_act_bf16(const void* y, const void* bias, const void* res, int64_t pixels, int c,
+                                 int relu, void* out, void* stream) {
+  if (pixels < 0 || c <= 0 || c % 8)
+    return fail(GPA_ERR_INVALID, "gpa_bias_act_bf16: channels must be a positive multiple of 8");
+  if (!y || !bias || !out || !aligned16(y) || !aligned16(bias) || !aligned16(out) || (res && !aligned16(res)))
+    return fail(GPA_ERR_INVALID, "gpa_bias_act_bf16: null or unaligned pointer");
+  const int64_t groups = pixels * (c / 8);
+  if (groups == 0) return ok();
+  const int64_t blocks = (groups + 255) / 256;
+  if (blocks > 0x7fffffffll) return fail(GPA_ERR_UNSUPPORTED, "gpa_bias_act_bf16: too large");
+  dpt::bias_act_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
+      (const __nv_bfloat16*)y, (const __nv_bfloat16*)bias, (const __nv_bfloat16*)res, c, groups, relu,
+      (__nv_bfloat16*)out);
+  return check_launch("gpa_bias_act_bf16");
+}
+

@@ -31,7 +31,8 @@ _DEVICE_STATUS = {}
 
 
 # When set to a list, every attention launch appends (start event, end event,
-# algorithmic flops, algorithmic bytes) recorded on its stream (bench.py's roofline).
+# algorithmic flops, algorithmic bytes, key count) recorded on its stream
+# (bench.py's roofline).
 ATTN_TIMING = None
 
 
@@ -334,7 +335,7 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bias: Optional[
              ptr(status), stream_of(q))
     if timing is not None:
         e1.record()
-        timing.append((e0, e1, 4.0 * B * H * M * N * D, 2.0 * B * H * (2 * M + 2 * N) * D))
+        timing.append((e0, e1, 4.0 * B * H * M * N * D, 2.0 * B * H * (2 * M + 2 * N) * D, N))
     if own:
         _check_status(status, "gpa_attention_keybias")
     return (out, lse) if return_lse else out
@@ -412,6 +413,23 @@ def upsample_bilinear_bf16(x: torch.Tensor, size, add: Optional[torch.Tensor] = 
          ptr(add), a_sh, a_sw, int(round_first), OH, OW, ptr(out), out.stride(0), out.stride(2),
          out.stride(3), stream_of(x))
     return out
+
+
+def bias_act(y: torch.Tensor, bias: torch.Tensor, res: Optional[torch.Tensor] = None,
+             relu: bool = False) -> torch.Tensor:
+    """In place on a channels-last bf16 map y [N, C, H, W]: bf16(y + bias),
+    then ReLU, then bf16(. + res) -- each rounded as torch's bf16 ops round."""
+    require_cuda(y, bias, res, what="bias_act")
+    cl = torch.channels_last
+    if (y.dtype != BF16 or y.dim() != 4 or not y.is_contiguous(memory_format=cl)
+            or (res is not None and (res.dtype != BF16 or res.shape != y.shape
+                                     or not res.is_contiguous(memory_format=cl)))):
+        raise ValueError("bias_act: channels-last contiguous bf16 maps of one shape required")
+    N, C, H, W = y.shape
+    b = bias.to(BF16).contiguous()
+    call("gpa_bias_act_bf16", ptr(y), ptr(b), ptr(res), N * H * W, C, int(bool(relu)), ptr(y),
+         stream_of(y))
+    return y
 
 
 def gelu(x: torch.Tensor) -> torch.Tensor:

@@ -98,7 +98,8 @@ class Aggregator(nn.Module):
         B, S, _, H, W = images.shape
         dt = self.camera_token.dtype
         x = ((images - self._resnet_mean) / self._resnet_std).to(dt).view(B * S, 3, H, W)
-        patch = self.patch_embed(x).to(dt)
+        with nvtx("dino_embed"):
+            patch = self.patch_embed(x).to(dt)
         f0 = self.shard.f0 if self.shard is not None else 0
         tokens = torch.cat([special_tokens(self.camera_token, B, S, f0),
                             special_tokens(self.register_token, B, S, f0), patch], 1).to(dt)
@@ -114,7 +115,8 @@ class Aggregator(nn.Module):
             gm = b if merge_window(b, self.merging, self.merge_end, self.early_frame_split,
                                    self.core_blocks, self.core_merge_ratio) else None
             attn = self.global_blocks[b].attn
-            kind = "frame_shared" if attn.frame_special else ("merged" if gm is not None else "global")
+            kind = ("frame_shared" if attn.frame_special else
+                    ("plain" if gm is None else ("core" if b in self.core_blocks else "merged")))
             with nvtx(f"global_block_{b}_{kind}"):
                 tokens = self.global_blocks[b](tokens.view(B, S * P, C), pos=pos.view(B, S * P, 2),
                                                global_merging=gm)

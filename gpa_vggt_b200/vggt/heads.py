@@ -116,6 +116,36 @@ def _fused_resize_ok(x) -> bool:
             and x.stride(1) == 1 and x.shape[1] % 8 == 0)
 
 
+# Convolutions of the head that carry a bias: on CUDA channels-last bf16 maps
+# under bf16 autocast, the convolution runs without its bias and one pass adds
+# the bias, the ReLU and the residual (kernels.bias_act), rounding as torch's
+# separate bf16 ops do; elsewhere the torch ops run.
+FUSED_CONV_EPILOGUE = True
+
+
+def _conv_act(conv, x, relu=False, res=None, transpose=False):
+    """conv(x), then ReLU if relu, then + res if res is given (torch semantics)."""
+    if (FUSED_CONV_EPILOGUE and conv.bias is not None and x.is_cuda and x.dim() == 4
+            and torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16
+            and conv.out_channels % 8 == 0 and conv.groups == 1):
+        if transpose:
+            y = F.conv_transpose2d(x, conv.weight, None, conv.stride, conv.padding,
+                                   conv.output_padding, conv.groups, conv.dilation)
+        else:
+            y = F.conv2d(x, conv.weight, None, conv.stride, conv.padding, conv.dilation, conv.groups)
+        cl = torch.channels_last
+        if (y.dtype == torch.bfloat16 and y.is_contiguous(memory_format=cl)
+                and (res is None or (res.dtype == torch.bfloat16 and res.shape == y.shape
+                                     and res.is_contiguous(memory_format=cl)))):
+            return kernels.bias_act(y, conv.bias, res, relu)
+        y = y + conv.bias.to(y.dtype)[None, :, None, None]   # the bias add torch would do
+    else:
+        y = conv(x)
+    if relu:
+        y = F.relu(y)
+    return y if res is None else y + res
+
+
 class ResidualConvUnit(nn.Module):
     """conv2(relu(conv1(relu(x)))) + relu(x): the reference's activation is an
     in-place ReLU applied to the unit's input, so its skip connection carries
@@ -128,7 +158,7 @@ class ResidualConvUnit(nn.Module):
 
     def forward(self, x):
         x = F.relu(x)
-        return self.conv2(F.relu(self.conv1(x))) + x
+        return _conv_act(self.conv2, _conv_act(self.conv1, x, relu=True), res=x)
 
 
 class FeatureFusionBlock(nn.Module):
@@ -151,7 +181,7 @@ class FeatureFusionBlock(nn.Module):
             out = kernels.upsample_bilinear_bf16(out, size)
         else:
             out = _interp(out, size=size)
-        return self.out_conv(out)
+        return _conv_act(self.out_conv, out)
 
 
 class DPTHead(nn.Module):
@@ -204,14 +234,21 @@ class DPTHead(nn.Module):
             x = tap[:, f0:f1, psi:].reshape(B * S, -1, tap.shape[-1])
             x = self.norm(x).permute(0, 2, 1).reshape(B * S, -1, ph, pw)
             x = self._pos(self.projects[i](x), W, H)
-            feats.append(self.resize_layers[i](x))
+            rl = self.resize_layers[i]
+            if isinstance(rl, nn.ConvTranspose2d):
+                x = _conv_act(rl, x, transpose=True)
+            elif isinstance(rl, nn.Conv2d):
+                x = _conv_act(rl, x)
+            else:
+                x = rl(x)
+            feats.append(x)
         sc = self.scratch
         l1, l2, l3, l4 = (getattr(sc, f"layer{i + 1}_rn")(f) for i, f in enumerate(feats))
         out = sc.refinenet4(l4, size=l3.shape[2:])
         out = sc.refinenet3(out, l3, size=l2.shape[2:])
         out = sc.refinenet2(out, l2, size=l1.shape[2:])
         out = sc.refinenet1(out, l1)
-        out = sc.output_conv1(out)
+        out = _conv_act(sc.output_conv1, out)
         size = (ph * self.patch_size, pw * self.patch_size)
         if _fused_resize_ok(out):
             # resize, the fp32 positional add and the conv's bf16 input cast in one
@@ -219,7 +256,9 @@ class DPTHead(nn.Module):
             fp32 = _autocast_resize_in_fp32(out.device)
             pe = self._pe_map(out.shape[1], size[0], size[1], torch.float32 if fp32 else out.dtype,
                               out.device, W, H)
-            out = sc.output_conv2(kernels.upsample_bilinear_bf16(out, size, add=pe, round_first=not fp32))
+            up = kernels.upsample_bilinear_bf16(out, size, add=pe, round_first=not fp32)
+            oc = sc.output_conv2
+            out = oc[2](_conv_act(oc[0], up, relu=True))
         else:
             out = _interp(out, size=size)
             out = sc.output_conv2(self._pos(out, W, H))

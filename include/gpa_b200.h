@@ -322,6 +322,18 @@ GPA_API int gpa_upsample_bilinear_bf16(const void* x, int x_dtype, int n, int c,
  * bf16(0.5 * x * (1 + erf(x / sqrt(2)))) in fp32 for n bf16 values, as torch
  * evaluates it for bf16 tensors.  n % 8 == 0, 16-byte aligned; out may alias x.
  */
+/*
+ * Bias, ReLU and residual after a DPT-head convolution, one pass over a
+ * channels-last bf16 map (replaces the bias add torch issues after each cuDNN
+ * convolution, the ReLU and the skip add of heads/dpt_head.py
+ * ResidualConvUnit): t = bf16(y + bias[c]); t = relu(t) if relu; out =
+ * bf16(t + res) if res.  Rounds as those torch ops do (bit-exact).  y, res,
+ * out: [pixels, c] bf16 contiguous (a channels-last map), c % 8 == 0, out may
+ * be y; bias: [c] bf16.
+ */
+GPA_API int gpa_bias_act_bf16(const void* y, const void* bias, const void* res, int64_t pixels, int c,
+                              int relu, void* out, void* stream);
+
 GPA_API int gpa_gelu_bf16(const void* x, int64_t n, void* out, void* stream);
 
 #ifdef __cplusplus

@@ -83,3 +83,41 @@ def test_dpt_fusion_block_matches_unfused_path():
             heads._fused_resize_ok = orig
     rel = float((fused.float() - plain.float()).norm() / plain.float().norm())
     assert rel < 2e-3
+
+
+@pytest.mark.parametrize("what", ["rcu", "fusion", "head"])
+def test_fused_conv_epilogue_matches_torch_ops(what):
+    """Convolutions without their bias, then one pass for bias + ReLU +
+    residual (gpa_bias_act_bf16), against the module's own torch ops: the
+    roundings are torch's (a bf16 bias add after the convolution, a bf16
+    residual add), so the outputs are equal."""
+    from gpa_vggt_b200.vggt import heads, init_weights
+    g = torch.Generator(device="cuda").manual_seed(11)
+    if what == "rcu":
+        mod = heads.ResidualConvUnit(64)
+        args = (_channels_last(2, 64, 24, 24, torch.bfloat16, g),)
+        kw = {}
+    elif what == "fusion":
+        mod = heads.FeatureFusionBlock(64)
+        args = (_channels_last(2, 64, 20, 20, torch.bfloat16, g), _channels_last(2, 64, 20, 20, torch.bfloat16, g))
+        kw = {"size": (37, 37)}
+    else:
+        mod = heads.DPTHead(dim_in=256, features=64, out_channels=(32, 64, 128, 128))
+        taps = [torch.randn(1, 2, 5 + 16 * 16, 256, device="cuda", generator=g).bfloat16() for _ in range(4)]
+        args = (taps,)
+        kw = {"images": torch.rand(1, 2, 3, 224, 224, device="cuda", generator=g), "patch_start_idx": 5}
+    init_weights(mod, seed=4)
+    mod = mod.cuda().bfloat16().to(memory_format=torch.channels_last)
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        fused = mod(*args, **kw)
+        heads.FUSED_CONV_EPILOGUE = False
+        try:
+            plain = mod(*args, **kw)
+        finally:
+            heads.FUSED_CONV_EPILOGUE = True
+    outs = fused if isinstance(fused, tuple) else (fused,)
+    refs = plain if isinstance(plain, tuple) else (plain,)
+    for a, b in zip(outs, refs):
+        d = (a.float() - b.float()).abs()
+        print(f"{what}: max |d| {float(d.max()):.3e}, {float((d > 0).float().mean()):.2e} of elements differ")
+        assert torch.equal(a, b)
