@@ -134,25 +134,34 @@ def merge_exchange(sh: FrameShard, rows: torch.Tensor, plan, tokens_per_frame: i
     seg = plan.seg_start.long()
     unm_owner = torch.div(src_pos[plan.unm_src.long()], LP, rounding_mode="floor")
     dst_owner = torch.div(dst_pos, LP, rounding_mode="floor")
-    mem_dst = torch.repeat_interleave(torch.arange(plan.num_dst, device=dev), seg[1:] - seg[:-1])
+    mem_dst = torch.repeat_interleave(torch.arange(plan.num_dst, device=dev), seg[1:] - seg[:-1],
+                                      output_size=plan.seg_src.numel())
     mem_src = plan.seg_src.long()
     mem_owner = dst_owner[mem_dst]
     mem_rank = torch.div(src_pos[mem_src], LP, rounding_mode="floor")
     move = mem_owner != mem_rank
     # one small device-to-host read: slot counts per rank and the row matrix
-    cnt = torch.cat([torch.bincount(unm_owner, minlength=world), torch.bincount(dst_owner, minlength=world),
-                     torch.bincount((mem_rank * world + mem_owner)[move], minlength=world * world)]).cpu()
+    # (counted with scatter-adds into fixed-size bins, which need no read)
+    def count(idx, bins, weight=None):
+        out = torch.zeros(bins, device=dev, dtype=torch.long)
+        w = torch.ones_like(idx) if weight is None else weight.long()
+        return out.scatter_add_(0, idx, w)
+    cnt = torch.cat([count(unm_owner, world), count(dst_owner, world),
+                     count(mem_rank * world + mem_owner, world * world, move)]).cpu()
     unm_cnt, dst_cnt = cnt[:world].tolist(), cnt[world:2 * world].tolist()
     mat = cnt[2 * world:].view(world, world)
     # send: this rank's member rows that other ranks' slots need, by owner rank
-    mine = (move & (mem_rank == rank)).nonzero().reshape(-1)
-    send_m = mine[torch.sort(mem_owner[mine], stable=True).indices]
+    # (a stable sort on the owner, others keyed past the end, then the known
+    # count: no further device-to-host read)
+    n_send, n_recv = int(mat[rank].sum()), int(mat[:, rank].sum())
+    key = torch.where(move & (mem_rank == rank), mem_owner, world)
+    send_m = torch.sort(key, stable=True).indices[:n_send]
     send = rows[src_pos[mem_src[send_m]] - base]
-    recv = torch.empty((int(mat[:, rank].sum()),) + tuple(rows.shape[1:]), device=dev, dtype=rows.dtype)
+    recv = torch.empty((n_recv,) + tuple(rows.shape[1:]), device=dev, dtype=rows.dtype)
     sh.all_to_all(recv, send, mat[:, rank].tolist(), mat[rank].tolist())
     # receive: the members of this rank's slots from elsewhere, by source rank
-    theirs = (move & (mem_owner == rank)).nonzero().reshape(-1)
-    recv_m = theirs[torch.sort(mem_rank[theirs], stable=True).indices]
+    key = torch.where(move & (mem_owner == rank), mem_rank, world)
+    recv_m = torch.sort(key, stable=True).indices[:n_recv]
     buf = torch.cat([rows, recv]) if recv.shape[0] else rows
     src_map = (src_pos - base).to(torch.int32)
     src_map[mem_src[recv_m]] = torch.arange(LP, LP + recv_m.numel(), device=dev, dtype=torch.int32)
