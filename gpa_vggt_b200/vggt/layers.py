@@ -10,6 +10,7 @@ evaluation does (eval/bench_e2e.py:90-95).
 from __future__ import annotations
 
 import math
+import os
 from typing import Optional
 
 import torch
@@ -236,12 +237,18 @@ def _merge_draws(attn: Attention, num_imgs: int, C: int, device, dtype):
     return rand_idx, proj
 
 
+# Sharded merged blocks attend to the rank's own merged slots while the other
+# ranks' merged rows are all-gathered (GPA_OVERLAP_GATHER=0: gather all merged
+# rows first, then one attention launch).
+OVERLAP_GATHER = os.environ.get("GPA_OVERLAP_GATHER", "1") == "1"
+
+
 def merged_attention_sharded(x, q, k, v, attn: Attention) -> torch.Tensor:
     """Merged block with the queries sharded by frame (see shard.py): every rank
     builds the same global plan from all-gathered match results, merges the
     output slots of its own frames (merge_exchange) and attends with its own
     queries against all merged keys."""
-    from .shard import merge_exchange
+    from .shard import merge_exchange, merge_local
     sh = attn.shard
     B, Nl, C = x.shape
     H, D = attn.num_heads, attn.head_dim
@@ -283,13 +290,39 @@ def merged_attention_sharded(x, q, k, v, attn: Attention) -> torch.Tensor:
     # K and V travel and merge as one [tokens, 2*H*D] row buffer (V widened to
     # K's dtype when they differ: exact, and the merged V is rounded back below)
     kv = torch.stack((k[0], v[0].to(k.dtype)), 1).reshape(Nl, 2 * H * D)
-    merged = merge_exchange(sh, kv, plan, P, kernels).view(plan.n_out, 2, H, D)
-    km, vm = merged[:, 0].to(BF16), merged[:, 1].to(BF16)
     bias = plan.counts.log().to(BF16).float()
     out = torch.empty(1, Nl, H, D, device=dev, dtype=BF16)
-    kernels.attention(q.to(BF16).permute(0, 2, 1, 3), km.permute(1, 0, 2)[None],
-                      vm.permute(1, 0, 2)[None], bias[None, None], attn.scale,
-                      out=out.permute(0, 2, 1, 3))
+    qh, oh = q.to(BF16).permute(0, 2, 1, 3), out.permute(0, 2, 1, 3)
+
+    def attend(merged, key_bias, **kw):
+        m = merged.view(merged.shape[0], 2, H, D)
+        kernels.attention(qh, m[:, 0].to(BF16).permute(1, 0, 2)[None],
+                          m[:, 1].to(BF16).permute(1, 0, 2)[None], key_bias[None, None],
+                          attn.scale, out=oh, **kw)
+
+    if not OVERLAP_GATHER:
+        attend(merge_exchange(sh, kv, plan, P, kernels), bias)
+        return out
+    # The rank's own merged slots are attended while the other ranks' merged
+    # rows arrive on the key/value communicator; the second launch attends the
+    # rest and combines both softmax partitions by log-sum-exp in its epilogue
+    # (attention is invariant to the order and partition of its keys).
+    own, (unm_cnt, dst_cnt, u0, e0) = merge_local(sh, kv, plan, P, kernels)
+    nu, nd, U = unm_cnt[sh.rank], dst_cnt[sh.rank], plan.unm_len
+    full, work = sh.gather_varlen2_async(own[:nu], own[nu:], unm_cnt, dst_cnt)
+    lse = torch.empty(1, H, Nl, device=dev, dtype=torch.float32)
+    attend(own, torch.cat([bias[u0:u0 + nu], bias[U + e0:U + e0 + nd]]), lse_out=lse)
+    work.wait()
+    ma = max(unm_cnt)
+    rows, key_bias = [], []
+    uu = ee = 0
+    for r in range(sh.world):
+        if r != sh.rank:
+            rows += [full[r, :unm_cnt[r]], full[r, ma:ma + dst_cnt[r]]]
+            key_bias += [bias[uu:uu + unm_cnt[r]], bias[U + ee:U + ee + dst_cnt[r]]]
+        uu += unm_cnt[r]
+        ee += dst_cnt[r]
+    attend(torch.cat(rows), torch.cat(key_bias), combine=(oh, lse))
     return out
 
 

@@ -85,6 +85,18 @@ class FrameShard:
         gb = torch.cat([full[i, ma: ma + counts_b[i]] for i in range(self.world)], 0)
         return ga, gb
 
+    def gather_varlen2_async(self, a: torch.Tensor, b: torch.Tensor, counts_a: Sequence[int],
+                             counts_b: Sequence[int]):
+        """gather_varlen2 started on the key/value communicator.  Returns (full,
+        work): after work.wait(), rank i's rows of a are full[i, :counts_a[i]]
+        and its rows of b full[i, max(counts_a):max(counts_a) + counts_b[i]]."""
+        ma, mb = max(counts_a), max(counts_b)
+        pad = torch.zeros((ma + mb,) + tuple(a.shape[1:]), device=a.device, dtype=a.dtype)
+        pad[: a.shape[0]] = a
+        pad[ma: ma + b.shape[0]] = b
+        full, work = self.gather_async(pad)
+        return full.view((self.world, ma + mb) + tuple(a.shape[1:])), work
+
     def gather_varlen(self, t: torch.Tensor, counts: Sequence[int]) -> torch.Tensor:
         """All-gather along dim 0 when rank i holds counts[i] rows."""
         m = max(counts)
@@ -116,16 +128,28 @@ class FrameShard:
 def merge_exchange(sh: FrameShard, rows: torch.Tensor, plan, tokens_per_frame: int,
                    kernels) -> torch.Tensor:
     """Merged rows of every output slot of `plan` (identical on every rank),
-    from this rank's token rows [local_frames * P, C].
+    from this rank's token rows [local_frames * P, C]: merge_local, then one
+    all-gather of every rank's merged rows in slot order.  Returns [N_m, C] in
+    rows' dtype."""
+    own, (unm_cnt, dst_cnt, _, _) = merge_local(sh, rows, plan, tokens_per_frame, kernels)
+    nu = unm_cnt[sh.rank]
+    unm_all, dst_all = sh.gather_varlen2(own[:nu], own[nu:], unm_cnt, dst_cnt)
+    return torch.cat([unm_all, dst_all])
+
+
+def merge_local(sh: FrameShard, rows: torch.Tensor, plan, tokens_per_frame: int, kernels):
+    """This rank's merged output slots of `plan`, from its token rows
+    [local_frames * P, C].
 
     Each output slot belongs to the rank whose frames hold its token (the
     unmerged src token, or the dst token); since ordinals are frame-major, a
     rank's slots are one contiguous range of unmerged slots and one of dst
     slots.  The members of a rank's dst slots that sit in other ranks' frames
     come over one all-to-all; the rank merges its slots with the same kernel
-    and summation order as one GPU would (bit-identical results), and one
-    all-gather gives every rank all merged rows in slot order.  Returns
-    [N_m, C] in rows' dtype."""
+    and summation order as one GPU would (bit-identical results).  Returns
+    (its merged rows: its unmerged slots, then its dst slots, in rows' dtype;
+    (unmerged slots per rank, dst slots per rank, its first unmerged slot, its
+    first dst slot))."""
     world, rank = sh.world, sh.rank
     dev = rows.device
     LP = sh.local * tokens_per_frame
@@ -174,6 +198,5 @@ def merge_exchange(sh: FrameShard, rows: torch.Tensor, plan, tokens_per_frame: i
     if nd:
         kernels.merge_kv_rows(buf, src_map, dst_map[e0:], None, plan.seg_start[e0:], plan.seg_src,
                               nd, out[nu:])
-    unm_all, dst_all = sh.gather_varlen2(out[:nu], out[nu:], unm_cnt, dst_cnt)
-    return torch.cat([unm_all, dst_all])
+    return out, (unm_cnt, dst_cnt, u0, e0)
 
