@@ -341,6 +341,9 @@ def main():
     for _ in range(args.warmup):
         step()
     barrier()
+    from gpa_vggt_b200 import nvtx as _nv
+    if _nv.TIMING:
+        _nv.block_times(reset=True)   # drop the warm-up steps' ranges
     kernels.ATTN_TIMING = []
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
@@ -356,7 +359,6 @@ def main():
         barrier()
         torch.cuda.profiler.stop()
     launches = _lib.launch_count() - l0
-    from gpa_vggt_b200 import nvtx as _nv
     if _nv.TIMING:   # per-range device ms of the timed steps, grouped by kind
         bt = _nv.block_times()
         kinds = {}

@@ -237,10 +237,13 @@ def _merge_draws(attn: Attention, num_imgs: int, C: int, device, dtype):
     return rand_idx, proj
 
 
-# Sharded merged blocks attend to the rank's own merged slots while the other
-# ranks' merged rows are all-gathered (GPA_OVERLAP_GATHER=0: gather all merged
-# rows first, then one attention launch).
-OVERLAP_GATHER = os.environ.get("GPA_OVERLAP_GATHER", "1") == "1"
+# GPA_OVERLAP_GATHER=1: sharded merged blocks attend to the rank's own merged
+# slots while the other ranks' merged rows are all-gathered, then combine the
+# two softmax partitions.  Off by default: at S=200 on 4 GPUs it saved 0.8% of
+# the forward, while the bf16 rounding of the first partition's output moved
+# the pose by 1.7e-2 (rel-L2) from the one-GPU forward, which the default path
+# (all merged rows first, one attention launch) reproduces exactly.
+OVERLAP_GATHER = os.environ.get("GPA_OVERLAP_GATHER", "0") == "1"
 
 
 def merged_attention_sharded(x, q, k, v, attn: Attention) -> torch.Tensor:

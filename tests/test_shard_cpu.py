@@ -60,15 +60,17 @@ class _Patch:
             setattr(obj, name, value)
 
 
-def _worker(rank, world, port, tmpdir):
+def _worker(rank, world, port, tmpdir, overlap=False):
     import sys
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     import cpu_kernels
+    from gpa_vggt_b200.vggt import layers
     from gpa_vggt_b200.vggt.shard import FrameShard
     cpu_kernels.install(setattr)
+    layers.OVERLAP_GATHER = overlap
     model = _model()
     shard = FrameShard(S)
     model.set_shard(shard)
@@ -88,7 +90,10 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_frame_sharded_forward_matches_unsharded(tmp_path):
+@pytest.mark.parametrize("overlap", [False, True])
+def test_frame_sharded_forward_matches_unsharded(tmp_path, overlap):
+    """overlap: merged blocks attend to own and gathered merged keys as two
+    partitions combined by log-sum-exp."""
     import cpu_kernels
     patch = _Patch()
     cpu_kernels.install(patch)
@@ -101,7 +106,7 @@ def test_frame_sharded_forward_matches_unsharded(tmp_path):
     finally:
         patch.undo()
     world = 2
-    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), overlap), nprocs=world,
                        start_method="spawn")
     for r in range(world):
         got = torch.load(tmp_path / OUT.format(r))
