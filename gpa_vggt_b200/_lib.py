@@ -43,6 +43,11 @@ SIGNATURES = {
     "gpa_merge_plan_noalloc": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp]),
     "gpa_merge_kv_mean": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_i64, _c_i64, _vp, _vp, _vp,
                                    _c_int, _vp, _vp, _c_int, _c_int, _vp, _vp, _c_i64, _c_i64, _vp]),
+    "gpa_ipc_export": (_c_int, [_vp, _vp, ctypes.POINTER(_c_i64)]),
+    "gpa_ipc_open": (_c_int, [_vp, _c_i64, ctypes.POINTER(_vp)]),
+    "gpa_ipc_close": (_c_int, [_vp, _c_i64]),
+    "gpa_merge_exchange_p2p": (_c_int, [_vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp,
+                                        _c_int, _vp, _vp, _c_int, _c_int, _c_int, _vp, _vp]),
     "gpa_attention_keybias": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,
                                        _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                                        _c_i64, _c_i64, _c_i64, _c_f32, _vp, _c_i64, _c_i64, _c_i64,

@@ -23,7 +23,8 @@ LIB = PKG / "libgpa_b200.so"
 OBJ = PKG / "_build"
 HEADER = ROOT / "include" / "gpa_b200.h"
 
-SOURCES = ["merge.cu", "sim_argmax.cu", "attention.cu", "frame.cu", "norm.cu", "dpt.cu", "proj.cu"]
+SOURCES = ["merge.cu", "sim_argmax.cu", "attention.cu", "frame.cu", "norm.cu", "dpt.cu", "proj.cu",
+           "exchange.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",

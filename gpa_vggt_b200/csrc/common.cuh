@@ -22,7 +22,8 @@ namespace gpa {
 // ---------------------------------------------------------------------------
 enum : int {
   kDevOk = 0,
-  kDevTimeout = 1,
+  kDevTimeout = 1,    // a pipeline wait gave up
+  kDevBadIndex = 2,   // an index outside its buffer (the access was skipped)
 };
 
 // A pipeline wait longer than this is treated as a lost signal (2 s).

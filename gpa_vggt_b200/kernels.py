@@ -51,14 +51,26 @@ def device_status_word(device) -> torch.Tensor:
     return w
 
 
+def _status_text(v: int) -> str:
+    """The device status bits: 1 = a pipeline wait gave up, 2 = an index
+    outside its buffer was skipped."""
+    parts = []
+    if v & 1:
+        parts.append("a kernel's pipeline wait gave up")
+    if v & 2:
+        parts.append("a kernel met an index outside its buffer")
+    return "; ".join(parts) or "unknown status"
+
+
 def check_device_status(device, what: str = "forward") -> None:
     """Read (synchronises) and clear the device's persistent status word;
-    raise KernelTimeout if a kernel recorded a wait that gave up."""
+    raise KernelTimeout if a kernel recorded a wait that gave up or skipped an
+    out-of-range index."""
     w = device_status_word(device)
     v = int(w.item())
     if v != 0:
         w.zero_()
-        raise KernelTimeout(f"{what}: device status {v} (a kernel's pipeline wait gave up; "
+        raise KernelTimeout(f"{what}: device status {v} ({_status_text(v)}; "
                             "its output is invalid)")
 
 
@@ -73,7 +85,7 @@ def _status_word(status, device):
 def _check_status(status, what):
     v = int(status.item())
     if v != 0:
-        raise KernelTimeout(f"{what}: device status {v} (a pipeline wait gave up)")
+        raise KernelTimeout(f"{what}: device status {v} ({_status_text(v)})")
 
 
 def wait_selftest(limit_ns: int, device="cuda") -> None:
@@ -264,6 +276,54 @@ def merge_kv_rows(rows: torch.Tensor, src_map: torch.Tensor, dst_map: Optional[t
          ptr(dst_map), ptr(unm_src), n_unm, ptr(seg_start), ptr(seg_src), int(num_dst), int(mean),
          None, ptr(out), 0, out.stride(0), stream_of(rows))
     return out
+
+
+def ipc_export(t: torch.Tensor):
+    """(64-byte CUDA IPC handle of t's allocation, t's byte offset in it)."""
+    require_cuda(t, what="ipc_export")
+    h = ctypes.create_string_buffer(64)
+    off = ctypes.c_int64(0)
+    call("gpa_ipc_export", ptr(t), h, ctypes.byref(off))
+    return h.raw, int(off.value)
+
+
+def ipc_open(handle: bytes, offset: int) -> int:
+    """This process's device address of a peer's exported byte (see ipc_export)."""
+    if len(handle) != 64:
+        raise ValueError("ipc_open: a 64-byte handle")
+    out = ctypes.c_void_p(0)
+    call("gpa_ipc_open", ctypes.create_string_buffer(handle, 64), ctypes.c_int64(offset),
+         ctypes.byref(out))
+    return int(out.value)
+
+
+def ipc_close(address: int, offset: int) -> None:
+    call("gpa_ipc_close", ctypes.c_void_p(address), ctypes.c_int64(offset))
+
+
+def merge_exchange_p2p(peer_rows: torch.Tensor, peer_out: torch.Tensor, rank: int, dtype: torch.dtype,
+                       rows_per_rank: int, row_elems: int, plan: "MergePlan", dst_lo: int,
+                       dst_hi: int, status: Optional[torch.Tensor] = None) -> None:
+    """Merge this rank's slots of `plan` from every rank's token rows and store
+    them into every rank's merged rows (gpa_merge_exchange_p2p).  peer_rows /
+    peer_out: int64 device tensors of the world's buffer addresses as this
+    process sees them; the rows buffers hold rows_per_rank rows of row_elems
+    `dtype` elements, the outputs plan.n_out rows.  The caller orders the
+    ranks' launches (a collective on the stream before and after)."""
+    require_cuda(peer_rows, peer_out, what="merge_exchange_p2p")
+    if peer_rows.dtype != torch.int64 or peer_out.dtype != torch.int64:
+        raise TypeError("merge_exchange_p2p: peer address tables are int64 tensors")
+    world = peer_rows.numel()
+    dt = _lib.GPA_DTYPE_BF16 if dtype == BF16 else (_lib.GPA_DTYPE_F32 if dtype == F32 else None)
+    if dt is None:
+        raise TypeError("merge_exchange_p2p: rows must be bf16 or fp32")
+    status, own = _status_word(status, peer_rows.device)
+    call("gpa_merge_exchange_p2p", ptr(peer_rows), ptr(peer_out), world, rank, dt, int(rows_per_rank),
+         int(row_elems), ptr(plan.src_pos), ptr(plan.dst_pos), ptr(plan.unm_src), plan.unm_len,
+         ptr(plan.seg_start), ptr(plan.seg_src), plan.num_dst, int(dst_lo), int(dst_hi), ptr(status),
+         stream_of(peer_rows))
+    if own:
+        _check_status(status, "gpa_merge_exchange_p2p")
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bias: Optional[torch.Tensor],

@@ -14,10 +14,12 @@ import os
 from typing import Optional
 
 import torch
+import torch.distributed as dist
 import torch.nn as nn
 import torch.nn.functional as F
 
 from .. import kernels
+from ..nvtx import nvtx
 from ..merging.merge import (build_plan, draw_dst_choice, fused_metric_ok, projection_basis,
                              projection_basis_t)
 
@@ -244,6 +246,10 @@ def _merge_draws(attn: Attention, num_imgs: int, C: int, device, dtype):
 # the pose by 1.7e-2 (rel-L2) from the one-GPU forward, which the default path
 # (all merged rows first, one attention launch) reproduces exactly.
 OVERLAP_GATHER = os.environ.get("GPA_OVERLAP_GATHER", "0") == "1"
+# Sharded merged blocks on CUDA with NCCL exchange their merged K/V through
+# peer memory in one kernel (merge_exchange_p2p); GPA_P2P_EXCHANGE=0 keeps the
+# NCCL all-to-all + merge + all-gather path (merge_exchange).
+P2P_EXCHANGE = os.environ.get("GPA_P2P_EXCHANGE", "1") == "1"
 
 
 def merged_attention_sharded(x, q, k, v, attn: Attention) -> torch.Tensor:
@@ -251,16 +257,87 @@ def merged_attention_sharded(x, q, k, v, attn: Attention) -> torch.Tensor:
     builds the same global plan from all-gathered match results, merges the
     output slots of its own frames (merge_exchange) and attends with its own
     queries against all merged keys."""
-    from .shard import merge_exchange, merge_local
+    from .shard import merge_exchange, merge_exchange_p2p, merge_local
     sh = attn.shard
     B, Nl, C = x.shape
     H, D = attn.num_heads, attn.head_dim
-    pw, ph, ns, g = attn.patch_width, attn.patch_height, attn.num_special, attn.merge_grid
-    P = pw * ph + ns
+    P = attn.patch_width * attn.patch_height + attn.num_special
     S, N = sh.frames, sh.frames * P
     if Nl != sh.local * P:
         raise ValueError("merged_attention_sharded: local tokens do not match the frame shard")
     dev = x.device
+    with nvtx("sharded_metric"):
+        a, b, dst_pos, src_pos, ranges = _sharded_metric(x, attn, S, C, P, dev)
+    with nvtx("sharded_gather_dst"):
+        b_full = sh.gather_varlen(b, [rd[1] - rd[0] for rd, _ in ranges])
+    (d0, d1), (s0, s1) = ranges[sh.rank]
+    with nvtx("sharded_sim"):
+        if s1 > s0:
+            nm, ni = kernels.sim_argmax(a[None], b_full[None])
+            nm, ni = nm[0], ni[0]
+        else:
+            nm = torch.empty(0, device=dev)
+            ni = torch.empty(0, device=dev, dtype=torch.int32)
+    with nvtx("sharded_gather_match"):
+        src_counts = [rs[1] - rs[0] for _, rs in ranges]
+        nm_full = sh.gather_varlen(nm, src_counts)
+        ni_full = sh.gather_varlen(ni, src_counts)
+    with nvtx("sharded_plan"):
+        plan = kernels.merge_plan(nm_full, ni_full, int(N * attn.merge_ratio), dst_pos, src_pos)
+    bias = plan.counts.log().to(BF16).float()
+    out = torch.empty(1, Nl, H, D, device=dev, dtype=BF16)
+    qh, oh = q.to(BF16).permute(0, 2, 1, 3), out.permute(0, 2, 1, 3)
+
+    def attend(merged, key_bias, **kw):
+        m = merged.view(merged.shape[0], 2, H, D)
+        with nvtx("sharded_attend"):
+            kernels.attention(qh, m[:, 0].to(BF16).permute(1, 0, 2)[None],
+                              m[:, 1].to(BF16).permute(1, 0, 2)[None], key_bias[None, None],
+                              attn.scale, out=oh, **kw)
+
+    if P2P_EXCHANGE and x.is_cuda and dist.get_backend(sh.group) == "nccl":
+        with nvtx("sharded_exchange"):
+            merged = merge_exchange_p2p(sh, k[0], v[0], plan, P, (d0, d1), kernels)
+        attend(merged, bias)
+        return out
+    # K and V travel and merge as one [tokens, 2*H*D] row buffer (V widened to
+    # K's dtype when they differ: exact, and the merged V is rounded back below)
+    kv = torch.stack((k[0], v[0].to(k.dtype)), 1).reshape(Nl, 2 * H * D)
+    if not OVERLAP_GATHER:
+        with nvtx("sharded_exchange"):
+            merged = merge_exchange(sh, kv, plan, P, kernels)
+        attend(merged, bias)
+        return out
+    # The rank's own merged slots are attended while the other ranks' merged
+    # rows arrive on the key/value communicator; the second launch attends the
+    # rest and combines both softmax partitions by log-sum-exp in its epilogue
+    # (attention is invariant to the order and partition of its keys).
+    with nvtx("sharded_exchange"):
+        own, (unm_cnt, dst_cnt, u0, e0) = merge_local(sh, kv, plan, P, kernels)
+        nu, nd, U = unm_cnt[sh.rank], dst_cnt[sh.rank], plan.unm_len
+        full, work = sh.gather_varlen2_async(own[:nu], own[nu:], unm_cnt, dst_cnt)
+    lse = torch.empty(1, H, Nl, device=dev, dtype=torch.float32)
+    attend(own, torch.cat([bias[u0:u0 + nu], bias[U + e0:U + e0 + nd]]), lse_out=lse)
+    work.wait()
+    ma = max(unm_cnt)
+    rows, key_bias = [], []
+    uu = ee = 0
+    for r in range(sh.world):
+        if r != sh.rank:
+            rows += [full[r, :unm_cnt[r]], full[r, ma:ma + dst_cnt[r]]]
+            key_bias += [bias[uu:uu + unm_cnt[r]], bias[U + ee:U + ee + dst_cnt[r]]]
+        uu += unm_cnt[r]
+        ee += dst_cnt[r]
+    attend(torch.cat(rows), torch.cat(key_bias), combine=(oh, lse))
+    return out
+
+
+def _sharded_metric(x, attn: Attention, S: int, C: int, P: int, dev):
+    """This rank's src and dst metric rows of a sharded merged block, the
+    roles' token positions and the per-rank ordinal ranges."""
+    sh = attn.shard
+    pw, ph, ns, g = attn.patch_width, attn.patch_height, attn.num_special, attn.merge_grid
+    Nl = x.shape[1]
     rand_idx, proj = _merge_draws(attn, S, C, dev, x.dtype)
     dst_pos, src_pos, slot = kernels.merge_roles(rand_idx, S, pw, ph, g, g, ns, False, dev)
     dpf = ns + (ph // g) * (pw // g)
@@ -279,54 +356,7 @@ def merged_attention_sharded(x, q, k, v, attn: Attention) -> torch.Tensor:
         if attn.merge_metric_dim and attn.merge_metric_dim < C:
             metric = metric @ proj.to(metric.dtype)
         a, b = kernels.metric_split(metric, src_pos[s0:s1] - base, dst_pos[d0:d1] - base)
-    b_full = sh.gather_varlen(b, [rd[1] - rd[0] for rd, _ in ranges])
-    if s1 > s0:
-        nm, ni = kernels.sim_argmax(a[None], b_full[None])
-        nm, ni = nm[0], ni[0]
-    else:
-        nm = torch.empty(0, device=dev)
-        ni = torch.empty(0, device=dev, dtype=torch.int32)
-    src_counts = [rs[1] - rs[0] for _, rs in ranges]
-    nm_full = sh.gather_varlen(nm, src_counts)
-    ni_full = sh.gather_varlen(ni, src_counts)
-    plan = kernels.merge_plan(nm_full, ni_full, int(N * attn.merge_ratio), dst_pos, src_pos)
-    # K and V travel and merge as one [tokens, 2*H*D] row buffer (V widened to
-    # K's dtype when they differ: exact, and the merged V is rounded back below)
-    kv = torch.stack((k[0], v[0].to(k.dtype)), 1).reshape(Nl, 2 * H * D)
-    bias = plan.counts.log().to(BF16).float()
-    out = torch.empty(1, Nl, H, D, device=dev, dtype=BF16)
-    qh, oh = q.to(BF16).permute(0, 2, 1, 3), out.permute(0, 2, 1, 3)
-
-    def attend(merged, key_bias, **kw):
-        m = merged.view(merged.shape[0], 2, H, D)
-        kernels.attention(qh, m[:, 0].to(BF16).permute(1, 0, 2)[None],
-                          m[:, 1].to(BF16).permute(1, 0, 2)[None], key_bias[None, None],
-                          attn.scale, out=oh, **kw)
-
-    if not OVERLAP_GATHER:
-        attend(merge_exchange(sh, kv, plan, P, kernels), bias)
-        return out
-    # The rank's own merged slots are attended while the other ranks' merged
-    # rows arrive on the key/value communicator; the second launch attends the
-    # rest and combines both softmax partitions by log-sum-exp in its epilogue
-    # (attention is invariant to the order and partition of its keys).
-    own, (unm_cnt, dst_cnt, u0, e0) = merge_local(sh, kv, plan, P, kernels)
-    nu, nd, U = unm_cnt[sh.rank], dst_cnt[sh.rank], plan.unm_len
-    full, work = sh.gather_varlen2_async(own[:nu], own[nu:], unm_cnt, dst_cnt)
-    lse = torch.empty(1, H, Nl, device=dev, dtype=torch.float32)
-    attend(own, torch.cat([bias[u0:u0 + nu], bias[U + e0:U + e0 + nd]]), lse_out=lse)
-    work.wait()
-    ma = max(unm_cnt)
-    rows, key_bias = [], []
-    uu = ee = 0
-    for r in range(sh.world):
-        if r != sh.rank:
-            rows += [full[r, :unm_cnt[r]], full[r, ma:ma + dst_cnt[r]]]
-            key_bias += [bias[uu:uu + unm_cnt[r]], bias[U + ee:U + ee + dst_cnt[r]]]
-        uu += unm_cnt[r]
-        ee += dst_cnt[r]
-    attend(torch.cat(rows), torch.cat(key_bias), combine=(oh, lse))
-    return out
+    return a, b, dst_pos, src_pos, ranges
 
 
 def merged_attention(x, q, k, v, attn: Attention) -> torch.Tensor:

@@ -192,6 +192,49 @@ GPA_API int gpa_merge_kv_mean(const void* t, int dtype, int heads, int n_tokens,
                       int64_t out_stride_n, void* stream);
 
 /*
+ * CUDA IPC for the peer-memory exchange below (no counterpart in the
+ * reference, which runs on one device).  gpa_ipc_export writes the 64-byte
+ * IPC handle of the device allocation holding ptr and ptr's byte offset in it;
+ * another process on the same node opens it with gpa_ipc_open, which returns
+ * that process's address of the same byte (peer access enabled lazily), and
+ * releases it with gpa_ipc_close(ptr, offset).  A process cannot open its own
+ * handle.
+ */
+#define GPA_IPC_HANDLE_BYTES 64
+GPA_API int gpa_ipc_export(const void* ptr, void* handle, int64_t* offset);
+GPA_API int gpa_ipc_open(const void* handle, int64_t offset, void** ptr);
+GPA_API int gpa_ipc_close(void* ptr, int64_t offset);
+
+/*
+ * The merged-block K/V exchange of the frame-sharded forward over NVLink peer
+ * memory, fused with the scatter-mean (merging/merge.py:234-250, merge.heads,
+ * whose slots the reference computes on one device; the collective itself has
+ * no counterpart in the reference).  World ranks each own rows_per_rank
+ * consecutive tokens; rank r's token rows (token t of the forward at row
+ * t - r*rows_per_rank, row_elems elements, contiguous rows) are at
+ * peer_rows[r], and every rank's merged output [unm_len + num_dst, row_elems]
+ * at peer_out[r] -- both DEVICE arrays of `world` pointers as this process
+ * addresses them (its own buffers and the peers' IPC mappings).  This rank
+ * merges the slots whose token it owns -- unmerged slots s with
+ * src_pos[unm_src[s]] in its rows, and dst slots [dst_lo, dst_hi) -- exactly as
+ * gpa_merge_kv_mean does (fp32 sums, dst row first, then members in ascending
+ * ordinal, divided by the count, rounded to dtype; bit-identical), reading
+ * member rows from whichever rank holds them and storing each merged row into
+ * every rank's output.  dtype GPA_DTYPE_BF16 or GPA_DTYPE_F32; row_elems % 8 ==
+ * 0, <= 2048; buffers 16-byte aligned; world <= 8.  Every rank's row buffer
+ * must be complete before any rank launches, and all launches finished before
+ * an output is read or a row buffer rewritten (the caller orders them, e.g.
+ * with a collective on the stream on both sides).  A token outside every
+ * rank's rows is skipped and sets bit 2 of *status (when status != NULL).
+ */
+GPA_API int gpa_merge_exchange_p2p(const void* const* peer_rows, void* const* peer_out, int world,
+                                   int rank, int dtype, int rows_per_rank, int row_elems,
+                                   const int32_t* src_pos, const int32_t* dst_pos,
+                                   const int32_t* unm_src, int unm_len, const int32_t* seg_start,
+                                   const int32_t* seg_src, int num_dst, int dst_lo, int dst_hi,
+                                   int* status, void* stream);
+
+/*
  * Flash attention with a per-key additive bias (replaces
  * merging/fused_attention.py:130-180, kernel _attn_keybias_kernel :70-127):
  *   o[b,h,i]   = sum_j softmax_j(q.k_j * sm_scale + bias[b,h,j]) v_j
@@ -318,11 +361,6 @@ GPA_API int gpa_upsample_bilinear_bf16(const void* x, int x_dtype, int n, int c,
                                        int64_t out_sw, void* stream);
 
 /*
- * Exact GELU of the MLP (vggt/layers/mlp.py, nn.GELU()): out[i] =
- * bf16(0.5 * x * (1 + erf(x / sqrt(2)))) in fp32 for n bf16 values, as torch
- * evaluates it for bf16 tensors.  n % 8 == 0, 16-byte aligned; out may alias x.
- */
-/*
  * Bias, ReLU and residual after a DPT-head convolution, one pass over a
  * channels-last bf16 map (replaces the bias add torch issues after each cuDNN
  * convolution, the ReLU and the skip add of heads/dpt_head.py
@@ -334,6 +372,11 @@ GPA_API int gpa_upsample_bilinear_bf16(const void* x, int x_dtype, int n, int c,
 GPA_API int gpa_bias_act_bf16(const void* y, const void* bias, const void* res, int64_t pixels, int c,
                               int relu, void* out, void* stream);
 
+/*
+ * Exact GELU of the MLP (vggt/layers/mlp.py, nn.GELU()): out[i] =
+ * bf16(0.5 * x * (1 + erf(x / sqrt(2)))) in fp32 for n bf16 values, as torch
+ * evaluates it for bf16 tensors.  n % 8 == 0, 16-byte aligned; out may alias x.
+ */
 GPA_API int gpa_gelu_bf16(const void* x, int64_t n, void* out, void* stream);
 
 #ifdef __cplusplus
