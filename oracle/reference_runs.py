@@ -152,9 +152,14 @@ class Composer:
         rope = R["RoPE"](frequency=100)
         self.block = _init(R["Block"](1024, 16, mlp_ratio=4.0, init_values=0.01, qk_norm=True,
                                       rope=rope), 0).eval()
-        self.x1 = torch.randn(1, P_TOK, 1024, generator=g)
-        self.pos1 = _positions(R, 1)
-        self.q1 = torch.randn(1, 16, P_TOK, 64, generator=g)
+        # the frame-local pieces run on a batch of up to 4 frames (the forward
+        # runs frame blocks batched over its frames; one frame's GEMMs are less
+        # efficient per token on some hosts) and are divided per frame
+        self.nf = min(S, 4)
+        self.x1 = torch.randn(self.nf, P_TOK, 1024, generator=g)
+        self.pos1 = _positions(R, 1).expand(self.nf, P_TOK, 2).contiguous()
+        self.qf = torch.randn(self.nf, 16, P_TOK, 64, generator=g)
+        self.q1 = self.qf[:1]
         N = S * P_TOK
         self.N = N
         nd = P_TOK + (S - 1) * 329
@@ -181,9 +186,9 @@ class Composer:
         with torch.no_grad():
             # a frame's tokens through one block (frame, DINO and the linears,
             # norms and MLP of a global block), and its own-frame attention
-            p["block_per_frame"] = _med(lambda: self.block(self.x1, pos=self.pos1), reps)
+            p["block_per_frame"] = _med(lambda: self.block(self.x1, pos=self.pos1), reps) / self.nf
             p["frame_sdpa_per_frame"] = _med(
-                lambda: F.scaled_dot_product_attention(self.q1, self.q1, self.q1), reps)
+                lambda: F.scaled_dot_product_attention(self.qf, self.qf, self.qf), reps) / self.nf
             if self.vanilla:
                 rq = 128
                 q = self.q1[:, :, :rq]

@@ -180,6 +180,8 @@ ATTN_CASES = [
     (1, 1, 256, 4000, True, True),
     (1, 16, 2048, 1500, True, False),
     (1, 2, 17, 5, True, True),
+    # short keys: persistent CTAs, each walking two or three work items
+    (40, 4, 260, 520, True, True),
 ]
 
 
