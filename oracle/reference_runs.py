@@ -264,8 +264,8 @@ class Composer:
 
 def composed_sample_note(S, vanilla):
     return (f"{'vanilla' if vanilla else 'GPA'} VGGT forward at S={S} composed from the reference's own "
-            f"CPU pieces (baseline/_ref, fp32, all host threads): a block on one frame's tokens, "
-            f"own-frame SDPA, the early blocks' SDPA with the shared set per frame, "
+            f"CPU pieces (baseline/_ref, fp32, all host threads): a block and the own-frame SDPA "
+            f"on a batch of up to 4 frames, the early blocks' SDPA with the shared set per frame, "
             f"token_merge_bipartite2d without its matcher at full size, fast_similarity_chunks on "
             f"1,000 src rows, merge.heads of K and V at full size, the masked SDPA on 128 query "
             f"rows, the DPT head on one frame, the camera head on S frames; scaled by rows/frames "
