@@ -20,7 +20,7 @@ def _rel(a, b):
     return float((a.double() - b.double()).norm() / b.double().norm())
 
 
-def _worker(rank, world, port, outdir, overlap):
+def _worker(rank, world, port, outdir, path):
     import sys
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -32,7 +32,8 @@ def _worker(rank, world, port, outdir, overlap):
     from bench import build_model, forward
     from gpa_vggt_b200.vggt import layers
     from gpa_vggt_b200.vggt.shard import FrameShard
-    layers.OVERLAP_GATHER = overlap
+    layers.P2P_EXCHANGE = path == "p2p"
+    layers.OVERLAP_GATHER = path == "nccl_overlap"
     dev = torch.device("cuda", rank)
     model = build_model(dev)
     images = torch.rand(1, S, 3, 518, 518, generator=torch.Generator().manual_seed(0)).to(torch.bfloat16)
@@ -51,14 +52,15 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("overlap", [False, True])
-def test_sharded_forward_matches_single_gpu(tmp_path, overlap):
-    """overlap: the merged blocks' attention split into own and gathered key
-    partitions combined by log-sum-exp; the first partition's bf16 output
-    rounding moves the pose by about 1.7e-2, so that path is held to the
-    model-level bound of 2e-2."""
+@pytest.mark.parametrize("path", ["p2p", "nccl", "nccl_overlap"])
+def test_sharded_forward_matches_single_gpu(tmp_path, path):
+    """The merged blocks' K/V exchange: p2p, the peer-memory kernel (default);
+    nccl, all-to-all + merge + all-gather; nccl_overlap, the merged blocks'
+    attention split into own and gathered key partitions combined by
+    log-sum-exp -- the first partition's bf16 output rounding moves the pose
+    by about 1.7e-2, so that path is held to the model-level bound of 2e-2."""
     world = 2
-    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), overlap), nprocs=world,
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), path), nprocs=world,
                        start_method="spawn")
     from bench import build_model, forward
     model = build_model(torch.device("cuda", 0))
@@ -69,5 +71,5 @@ def test_sharded_forward_matches_single_gpu(tmp_path, overlap):
         e_pose = _rel(got["pose"], pose.float().cpu())
         e_depth = _rel(got["depth"], depth[:, got["f0"]:got["f1"]].float().cpu())
         print(f"rank {r}: rel-L2 pose {e_pose:.2e} depth {e_depth:.2e}")
-        bound = 2e-2 if overlap else 1e-2
+        bound = 2e-2 if path == "nccl_overlap" else 1e-2
         assert e_pose < bound and e_depth < bound
