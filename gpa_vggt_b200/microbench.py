@@ -1,6 +1,6 @@
 """Kernel microbenchmarks (one JSON line per case), each against its roofline.
 
-    python -m gpa_vggt_b200.microbench attn  --lq 274800 --lk 66845 [--heads 16] [--no-bias]
+    python -m gpa_vggt_b200.microbench attn  --lq 274800 --lk 66845 [--heads 16] [--no-bias] [--batch 1]
     python -m gpa_vggt_b200.microbench sim   --m 131072 --n 131072 [--d 128]
     python -m gpa_vggt_b200.microbench merge --frames 200 [--ratio 0.98]
     python -m gpa_vggt_b200.microbench pool  --frames 200
@@ -82,20 +82,22 @@ def merged_len(S, ratio=0.98):
     return nd if r >= ns else ns - r + nd
 
 
-def bench_attn(lq, lk, heads=16, bias=True, iters=5, warmup=2, seed=0):
+def bench_attn(lq, lk, heads=16, bias=True, iters=5, warmup=2, seed=0, batch=1):
+    """batch > 1: independent sequences (e.g. the frame attention, one per frame)."""
     dev = torch.device("cuda")
     g = torch.Generator(device=dev).manual_seed(seed)
-    q = torch.randn(1, heads, lq, 64, device=dev, generator=g).bfloat16()
-    k = torch.randn(1, heads, lk, 64, device=dev, generator=g).bfloat16()
-    v = torch.randn(1, heads, lk, 64, device=dev, generator=g).bfloat16()
-    b = (1 + torch.poisson(torch.ones(lk, device=dev), generator=g)).log()[None, None] if bias else None
+    q = torch.randn(batch, heads, lq, 64, device=dev, generator=g).bfloat16()
+    k = torch.randn(batch, heads, lk, 64, device=dev, generator=g).bfloat16()
+    v = torch.randn(batch, heads, lk, 64, device=dev, generator=g).bfloat16()
+    b = ((1 + torch.poisson(torch.ones(batch, 1, lk, device=dev), generator=g)).log().expand(batch, heads, lk)
+         if bias else None)
     out = torch.empty_like(q)
     status = torch.zeros(1, device=dev, dtype=torch.int32)
     ms = timed(lambda: kernels.attention(q, k, v, b, 0.125, out=out, status=status), iters, warmup)
-    flops = 4.0 * lq * lk * 64 * heads
+    flops = 4.0 * batch * lq * lk * 64 * heads
     _, peak, src = peaks()
     tf = flops / ms / 1e9
-    return {"kernel": "attention", "lq": lq, "lk": lk, "heads": heads, "bias": bias, "ms": ms,
+    return {"kernel": "attention", "batch": batch, "lq": lq, "lk": lk, "heads": heads, "bias": bias, "ms": ms,
             "tflops": tf, "peak_tflops": peak, "frac": tf / peak, "peak_src": src,
             "status": int(status.item()), "clocks": dict(LAST_CLOCKS)}
 
@@ -163,6 +165,7 @@ def main(argv=None):
     ap.add_argument("--lq", type=int, default=200 * P_TOK)
     ap.add_argument("--lk", type=int, default=merged_len(200))
     ap.add_argument("--heads", type=int, default=16)
+    ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-bias", action="store_true")
     ap.add_argument("--m", type=int, default=131072)
     ap.add_argument("--n", type=int, default=131072)
@@ -175,7 +178,7 @@ def main(argv=None):
     _lib.load()
     rows = []
     if a.what == "attn":
-        rows.append(bench_attn(a.lq, a.lk, a.heads, not a.no_bias, a.iters, a.warmup))
+        rows.append(bench_attn(a.lq, a.lk, a.heads, not a.no_bias, a.iters, a.warmup, batch=a.batch))
     elif a.what == "sim":
         rows.append(bench_sim(a.m, a.n, a.d, a.iters, a.warmup))
     elif a.what == "merge":
