@@ -84,3 +84,33 @@ def test_argument_errors_of_the_block_kernels(lib):
     A = _lib.i64array
     assert lib.gpa_lse_combine(2, 2, 4, 64, ok, A([64, 512, 4]), ok, A([8, 4, 1]), ok, A([64, 512, 128]),
                                ok, A([8, 4, 1]), ok, A([64, 512, 128]), None) == 1
+
+
+def test_argument_errors_of_the_exchange_entry_points(lib):
+    """The peer-memory exchange and its IPC helpers reject bad arguments before
+    any CUDA call (so this runs without a GPU)."""
+    I, I64, P = ctypes.c_int, ctypes.c_int64, ctypes.c_void_p
+    fake = P(16)   # never dereferenced: every call below fails validation first
+
+    def xch(world, rank, dtype, rows, elems, unm, nd, lo, hi, seg_src=fake):
+        return lib.gpa_merge_exchange_p2p(fake, fake, I(world), I(rank), I(dtype), I(rows), I(elems),
+                                          fake, fake, fake, I(unm), fake, seg_src, I(nd), I(lo), I(hi),
+                                          None, None)
+    assert xch(0, 0, 1, 10, 2048, 0, 4, 0, 4) == 1            # world < 1
+    assert xch(9, 0, 1, 10, 2048, 0, 4, 0, 4) == 1            # world > 8
+    assert xch(2, 2, 1, 10, 2048, 0, 4, 0, 4) == 1            # rank outside the world
+    assert b"world" in lib.gpa_last_error()
+    assert xch(2, 0, 1, 10, 2052, 0, 4, 0, 4) == 3            # row not a multiple of 8
+    assert xch(2, 0, 1, 10, 4096, 0, 4, 0, 4) == 3            # row above 2048 elements
+    assert xch(2, 0, 7, 10, 2048, 0, 4, 0, 4) == 1            # dtype
+    assert xch(2, 0, 1, 10, 2048, 0, 4, 3, 2) == 1            # dst range reversed
+    assert xch(2, 0, 1, 10, 2048, 0, 4, 0, 5) == 1            # dst range past num_dst
+    assert xch(2, 0, 1, 0, 2048, 0, 4, 0, 4) == 1             # no rows per rank
+    assert xch(2, 0, 1, 10, 2048, 0, 4, 0, 4, seg_src=None) == 1   # null member list
+    assert b"null" in lib.gpa_last_error()
+    assert lib.gpa_merge_exchange_p2p(P(17), fake, I(2), I(0), I(1), I(10), I(2048), fake, fake, fake,
+                                      I(0), fake, fake, I(4), I(0), I(4), None, None) == 1   # unaligned table
+    assert lib.gpa_ipc_export(None, None, None) == 1
+    assert lib.gpa_ipc_open(None, I64(0), None) == 1
+    assert lib.gpa_ipc_open(ctypes.create_string_buffer(64), I64(-1), ctypes.byref(P())) == 1
+    assert lib.gpa_ipc_close(None, I64(0)) == 1
