@@ -437,7 +437,8 @@ def main():
 
     pk = peaks()
     achieved = attn_flops / (attn_ms * 1e-3) / 1e12
-    roof = {"kernel": "attn_kernel (gpa_attention_keybias), all launches of a step",
+    roof = {"kernel": "attention kernels (gpa_attention_keybias: attn_kernel, and attn_persistent_kernel "
+                      "for short key sequences), all launches of a step",
             "bound": "tensor", "achieved": achieved, "peak": pk["bf16_sus"], "unit": "TFLOP/s",
             "frac": achieved / pk["bf16_sus"], "peak_kind": f"{pk['src']} sustained bf16 (long step)",
             "frac_of_burst": achieved / pk["bf16"], "flops_per_step": attn_flops,
